@@ -1,0 +1,169 @@
+/*
+ * qmm.h -- C ABI of the B200 (sm_100a) quantized-matmul library (libqmm.so).
+ *
+ * Drop-in device path for the quantized-matmul hot path of
+ * sweengineeringlabs/machinelearning (crate swe-llmmodel-kernel, called from
+ * Linear::forward). Every entry point is `extern "C"`, takes plain pointers and
+ * sizes, returns a qmm_status, never throws, never aborts the process, and
+ * frees only what it allocated (conventions of the reference's FFI crate,
+ * llminference/main/features/inference/ffi/main/src/lib.rs:12-40).
+ *
+ * Reference files cited below are paths inside the reference project.
+ *
+ * Weights are the raw GGUF / quantizer block bytes, uploaded unchanged:
+ *   Q8_0 (id 8)  34 B / 32 values  [f16 d][32 x i8]            d*q
+ *   Q4_0 (id 2)  18 B / 32 values  [f16 d][16 nibble bytes]    d*(n-8)
+ *   Q4_1 (id 3)  20 B / 32 values  [f16 d][f16 m][16 nibble bytes]  d*n+m
+ * Nibble order is GGML's (low nibble of byte j = element j, high = j+16), the
+ * order every reference matmul reads (simd.rs:30-52).
+ */
+#ifndef QMM_H
+#define QMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QMM_API __attribute__((visibility("default")))
+
+/* Status codes. 1-4 mirror QuantError (kernel/main/src/api/error.rs:5-18). */
+typedef enum qmm_status {
+    QMM_OK = 0,
+    QMM_ERR_BLOCK_ALIGNMENT = 1, /* in_features (or element count) not a multiple of 32 */
+    QMM_ERR_SHAPE_MISMATCH = 2,  /* a buffer is shorter than the shape needs (the reference panics) */
+    QMM_ERR_DTYPE_MISMATCH = 3,  /* unknown or unsupported block type */
+    QMM_ERR_INVALID_DATA = 4,
+    QMM_ERR_CUDA = 5,            /* a CUDA call failed; see qmm_last_error_message() */
+    QMM_ERR_NCCL = 6,
+    QMM_ERR_TIMEOUT = 7,         /* a bounded device-side wait gave up (see qmm_device_error) */
+    QMM_ERR_INVALID_INPUT = 8,   /* null pointer, misaligned pointer, bad enum */
+    QMM_ERR_NO_DEVICE = 9        /* no CUDA device / the library's kernels cannot run here */
+} qmm_status;
+
+/* Block types (GGML ids, gguf/main/src/api/types.rs:8-12). */
+typedef enum qmm_dtype { QMM_Q4_0 = 2, QMM_Q4_1 = 3, QMM_Q8_0 = 8 } qmm_dtype;
+
+/* Activation handling, the reference's Linear flags (linear.rs:24-29):
+ *   QMM_ACT_F32  : f32 activations x dequantised weights   (matmul_f32_q4 / _q8 / _q4_1)
+ *   QMM_ACT_Q8_0 : activations quantised to Q8_0, integer block dots
+ *                  (matmul_f32_q4_native / _q8_v2 / _q4_1_native; use_native_q4/q8 = true).
+ *                  Q8_0 weights use quantize_q8_0 (quantize.rs:451), Q4 weights use
+ *                  quantize_row_q8_0 (quantize.rs:676), exactly as the reference. */
+typedef enum qmm_act { QMM_ACT_F32 = 0, QMM_ACT_Q8_0 = 1 } qmm_act;
+
+QMM_API int qmm_version(void);
+QMM_API const char* qmm_status_string(int status);
+/* Detail of the last failing call on this host thread ("" if none). */
+QMM_API const char* qmm_last_error_message(void);
+/* Number of CUDA devices the library can use (0 on a host without GPUs). */
+QMM_API int qmm_device_count(void);
+/* Reads and clears the device-side error word of `device` (0 = none, 1 = a
+ * bounded wait timed out). Synchronises the device. */
+QMM_API int qmm_device_error(int device, int* out_error);
+
+/* ------------------------------------------------------------------------
+ * Reference-signature host entry points. Host buffers in, host buffers out,
+ * exactly the arguments of the Rust functions they replace; `output` holds
+ * m*out_features floats. Each call runs on the current CUDA device and
+ * synchronises. If `weight_bytes` was registered with
+ * qmm_register_host_weight(), its resident device copy is used; otherwise the
+ * weights are copied to the device for this call.
+ * ------------------------------------------------------------------------ */
+/* matmul_f32_q8 (quantize.rs:297-303) */
+QMM_API int qmm_matmul_f32_q8(const float* input_data, size_t input_len, const uint8_t* weight_bytes,
+                              size_t weight_len, size_t m, size_t in_features, size_t out_features,
+                              float* output);
+/* matmul_f32_q8_v2 (quantize.rs:429-435) */
+QMM_API int qmm_matmul_f32_q8_v2(const float* input_data, size_t input_len, const uint8_t* weight_bytes,
+                                 size_t weight_len, size_t m, size_t in_features, size_t out_features,
+                                 float* output);
+/* matmul_f32_q4 (quantize.rs:535-541) */
+QMM_API int qmm_matmul_f32_q4(const float* input_data, size_t input_len, const uint8_t* weight_bytes,
+                              size_t weight_len, size_t m, size_t in_features, size_t out_features,
+                              float* output);
+/* matmul_f32_q4_native (quantize.rs:646-652) */
+QMM_API int qmm_matmul_f32_q4_native(const float* input_data, size_t input_len, const uint8_t* weight_bytes,
+                                     size_t weight_len, size_t m, size_t in_features, size_t out_features,
+                                     float* output);
+/* matmul_f32_q4_1 (quantize.rs:807-813) */
+QMM_API int qmm_matmul_f32_q4_1(const float* input_data, size_t input_len, const uint8_t* weight_bytes,
+                                size_t weight_len, size_t m, size_t in_features, size_t out_features,
+                                float* output);
+/* matmul_f32_q4_1_native (quantize.rs:938-944) */
+QMM_API int qmm_matmul_f32_q4_1_native(const float* input_data, size_t input_len, const uint8_t* weight_bytes,
+                                       size_t weight_len, size_t m, size_t in_features, size_t out_features,
+                                       float* output);
+
+/* quantize_q8_0 (quantize.rs:15-48): n % 32 == 0, out holds n/32*34 bytes. */
+QMM_API int qmm_quantize_q8_0(const float* data, size_t n, uint8_t* out);
+/* quantize_q4_0 (quantize.rs:124-165, interleaved nibble packing as the reference writes it). */
+QMM_API int qmm_quantize_q4_0(const float* data, size_t n, uint8_t* out);
+/* quantize_q4_1 (quantize.rs:207-251). */
+QMM_API int qmm_quantize_q4_1(const float* data, size_t n, uint8_t* out);
+/* quantize_row_q8_0 (quantize.rs:260-289): also writes the f32(f16) scales (n/32 floats). */
+QMM_API int qmm_quantize_row_q8_0(const float* input, size_t n, uint8_t* out, float* scales);
+/* Tensor::to_f32 for block types (tensor.rs:527-630; Q4_0 in GGML order). */
+QMM_API int qmm_dequantize(int dtype, const uint8_t* raw, size_t raw_len, size_t n_elements, float* out);
+
+/* Registers a host weight buffer (e.g. an mmap'd GGUF tensor, tensor.rs:405-414)
+ * whose bytes are uploaded once to the current device and reused by the
+ * reference-signature calls above for as long as it stays registered. The
+ * caller must not change those bytes while registered. */
+QMM_API int qmm_register_host_weight(const uint8_t* weight_bytes, size_t weight_len, int dtype, size_t n, size_t k);
+QMM_API int qmm_unregister_host_weight(const uint8_t* weight_bytes);
+
+/* ------------------------------------------------------------------------
+ * Device API (the hot path). Pointers ending in _dev are device pointers;
+ * `stream` is a cudaStream_t (NULL = legacy default stream). Calls are
+ * asynchronous on `stream` and do not synchronise.
+ * ------------------------------------------------------------------------ */
+typedef struct qmm_weight qmm_weight;
+
+/* Uploads an [n, k] block matrix (n rows of k/32 blocks, the GGUF layout) to
+ * `device` with one host-to-device copy, byte for byte, no repacking. */
+QMM_API int qmm_weight_create(int dtype, size_t n, size_t k, const uint8_t* host_bytes, size_t len, int device,
+                              qmm_weight** out);
+/* Same, from bytes already on `device` (device-to-device copy). */
+QMM_API int qmm_weight_create_from_device(int dtype, size_t n, size_t k, const uint8_t* dev_bytes, size_t len,
+                                          int device, qmm_weight** out);
+QMM_API int qmm_weight_destroy(qmm_weight* w);
+QMM_API int qmm_weight_info(const qmm_weight* w, int* dtype, size_t* n, size_t* k, const uint8_t** dev_bytes,
+                            int* device);
+
+/* y_dev[m, n] = x_dev[m, k] . W^T on the weight's device, workspace managed by
+ * the library (one buffer per device and stream, grown on demand with
+ * cudaMalloc; grow it with qmm_reserve_workspace before capturing a graph). */
+QMM_API int qmm_linear_forward(const qmm_weight* w, const float* x_dev, size_t m, float* y_dev, int act,
+                               void* stream);
+/* Host-buffer variant of qmm_linear_forward: copies x in and y out on `stream`
+ * (pinned buffers make the copies asynchronous) and synchronises the stream. */
+QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, size_t m, float* y_host, int act,
+                                    void* stream);
+QMM_API int qmm_reserve_workspace(int device, void* stream, size_t bytes);
+
+/* Fully caller-managed form: raw device weight bytes and a caller workspace of
+ * at least qmm_workspace_size() bytes (256-byte aligned, not shared by
+ * concurrent calls). w_dev must be 16-byte aligned. */
+QMM_API size_t qmm_workspace_size(int dtype, int act, size_t m, size_t n, size_t k);
+QMM_API int qmm_matmul_dev(int dtype, int act, const float* x_dev, const uint8_t* w_dev, size_t w_len, size_t m,
+                           size_t k, size_t n, float* y_dev, void* workspace_dev, size_t workspace_bytes,
+                           void* stream);
+
+/* Device quantisers, bit-identical to the reference's:
+ *   variant 0: quantize_q8_0   (unrounded inverse scale), dtype QMM_Q8_0
+ *   variant 1: quantize_row_q8_0 (f16-rounded inverse scale), dtype QMM_Q8_0; scales_dev optional
+ *   dtype QMM_Q4_0 / QMM_Q4_1: quantize_q4_0 / quantize_q4_1 (variant ignored). */
+QMM_API int qmm_quantize_dev(int dtype, int variant, const float* x_dev, size_t n, uint8_t* out_dev,
+                             float* scales_dev, void* stream);
+/* Device dequantiser with Tensor::to_f32 semantics. */
+QMM_API int qmm_dequantize_dev(int dtype, const uint8_t* w_dev, size_t w_len, size_t n_elements, float* out_dev,
+                               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMM_H */

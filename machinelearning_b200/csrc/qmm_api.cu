@@ -1,0 +1,526 @@
+// C ABI of libqmm.so (declared in include/qmm.h).
+//
+// Conventions follow the reference's FFI crate
+// (llminference/main/features/inference/ffi/main/src/lib.rs:12-40): status
+// codes instead of panics/exceptions, null checks on every pointer, the library
+// frees what it allocates, concurrent calls are allowed (shared state is behind
+// mutexes; per-stream workspaces keep concurrent streams apart).
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/qmm.h"
+#include "qmm_common.cuh"
+#include "qmm_kernels.cuh"
+
+using namespace qmm;
+
+// Device-side error word (one per device context). Kernels receive its address.
+__device__ int g_qmm_device_error = 0;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int status, const std::string& msg) {
+    t_last_error = msg;
+    return status;
+}
+int cuda_fail(cudaError_t e, const char* where) {
+    cudaGetLastError();  // clear sticky-free errors so later calls are not poisoned
+    return fail(QMM_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+#define QMM_CUDA(call)                                  \
+    do {                                                \
+        cudaError_t _e = (call);                        \
+        if (_e != cudaSuccess) return cuda_fail(_e, #call); \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (dev >= 0 && dev != prev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool valid_dtype(int dt) { return dt == QMM_Q4_0 || dt == QMM_Q4_1 || dt == QMM_Q8_0; }
+
+int num_sms(int dev) {
+    static std::mutex mu;
+    static std::map<int, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(dev);
+    if (it != cache.end()) return it->second;
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev] = v;
+    return v;
+}
+
+int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) return -1;
+    return d;
+}
+
+// ---- per-(device, stream) workspaces ---------------------------------------------
+struct Buffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_ws_mu;
+std::map<std::pair<int, void*>, Buffer> g_ws;
+
+int get_workspace(int dev, void* stream, size_t need, void** out) {
+    std::lock_guard<std::mutex> lock(g_ws_mu);
+    Buffer& b = g_ws[{dev, stream}];
+    if (b.bytes < need) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing((cudaStream_t)stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+            return fail(QMM_ERR_INVALID_INPUT,
+                        "workspace must grow during stream capture; call qmm_reserve_workspace first");
+        if (b.ptr) {
+            cudaStreamSynchronize((cudaStream_t)stream);
+            cudaFree(b.ptr);
+            b.ptr = nullptr;
+            b.bytes = 0;
+        }
+        size_t want = need < (1u << 20) ? (1u << 20) : need;
+        QMM_CUDA(cudaMalloc(&b.ptr, want));
+        QMM_CUDA(cudaMemset(b.ptr, 0, want));
+        b.bytes = want;
+    }
+    *out = b.ptr;
+    return QMM_OK;
+}
+
+// ---- shape helpers ----------------------------------------------------------------
+constexpr size_t kMaxGemvRows = 64;
+
+size_t row_bytes_of(int dt, size_t k) { return (k / QK) * (size_t)block_bytes(dt); }
+
+int check_shape(int dt, size_t m, size_t k, size_t n, size_t w_len) {
+    if (!valid_dtype(dt)) return fail(QMM_ERR_DTYPE_MISMATCH, "unsupported block type id");
+    if (k % QK) return fail(QMM_ERR_BLOCK_ALIGNMENT, "in_features not divisible by block size 32");
+    if (k == 0 || n > (size_t)INT32_MAX || k > (size_t)INT32_MAX || m > (size_t)INT32_MAX)
+        return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    if (w_len < n * row_bytes_of(dt, k)) return fail(QMM_ERR_SHAPE_MISMATCH, "weight buffer shorter than n*k/32 blocks");
+    return QMM_OK;
+}
+
+size_t workspace_for(int dt, int act, size_t m, size_t n, size_t k, int dev) {
+    if (m == 0 || n == 0) return 0;
+    const size_t rows = m < kMaxGemvRows ? m : kMaxGemvRows;
+    GemvPlan p;
+    if (!gemv_plan(dt, act == QMM_ACT_Q8_0, (int)rows, (int)n, (int)k, num_sms(dev), &p)) return 0;
+    return gemv_workspace_bytes(p);
+}
+
+// The device matmul: GEMV in chunks of <= 64 activation rows.
+int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size_t k, size_t n, float* y,
+               void* ws, size_t ws_bytes, cudaStream_t st) {
+    if (m == 0 || n == 0) return QMM_OK;
+    const int dev = current_device();
+    if (dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    int* err = device_error_word(dev);
+    for (size_t r0 = 0; r0 < m; r0 += kMaxGemvRows) {
+        const size_t rows = (m - r0) < kMaxGemvRows ? (m - r0) : kMaxGemvRows;
+        GemvPlan p;
+        if (!gemv_plan(dt, act == QMM_ACT_Q8_0, (int)rows, (int)n, (int)k, num_sms(dev), &p))
+            return fail(QMM_ERR_SHAPE_MISMATCH, "shape not supported");
+        if (gemv_workspace_bytes(p) > ws_bytes) return fail(QMM_ERR_INVALID_INPUT, "workspace too small");
+        GemvWorkspace w_s;
+        gemv_workspace_carve(p, ws, &w_s);
+        cudaError_t e = launch_gemv(p, w, x + r0 * k, y + r0 * n, w_s, err, st);
+        if (e != cudaSuccess) return cuda_fail(e, "launch_gemv");
+    }
+    return QMM_OK;
+}
+
+}  // namespace
+
+namespace qmm {
+int* device_error_word(int device) {
+    static std::mutex mu;
+    static std::map<int, int*> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(device);
+    if (it != cache.end()) return it->second;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_qmm_device_error) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    cache[device] = static_cast<int*>(p);
+    return static_cast<int*>(p);
+}
+}  // namespace qmm
+
+struct qmm_weight {
+    int dtype;
+    size_t n, k;
+    int device;
+    uint8_t* dev;
+    size_t len;
+};
+
+namespace {
+std::mutex g_reg_mu;
+std::map<const uint8_t*, qmm_weight*> g_registered;
+
+int weight_create_impl(int dtype, size_t n, size_t k, const uint8_t* src, size_t len, int device, bool from_device,
+                       qmm_weight** out) {
+    if (!out || !src) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    *out = nullptr;
+    int rc = check_shape(dtype, 0, k, n, len);
+    if (rc) return rc;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    }
+    if (device < 0 || device >= ndev) return fail(QMM_ERR_INVALID_INPUT, "bad device index");
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    const size_t bytes = n * row_bytes_of(dtype, k);
+    uint8_t* d = nullptr;
+    QMM_CUDA(cudaMalloc(&d, (bytes + 15) & ~size_t(15)));
+    cudaError_t e = cudaMemcpy(d, src, bytes, from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return cuda_fail(e, "weight upload");
+    }
+    qmm_weight* w = new qmm_weight{dtype, n, k, device, d, bytes};
+    *out = w;
+    return QMM_OK;
+}
+
+int act_for(bool native) { return native ? QMM_ACT_Q8_0 : QMM_ACT_F32; }
+
+// Shared body of the reference-signature host calls.
+int host_matmul(int dt, bool native, const float* x, size_t x_len, const uint8_t* w, size_t w_len, size_t m, size_t k,
+                size_t n, float* y) {
+    if (!x || !w || !y) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    int rc = check_shape(dt, m, k, n, w_len);
+    if (rc) return rc;
+    if (x_len < m * k) return fail(QMM_ERR_SHAPE_MISMATCH, "input shorter than m*in_features");
+    if (m == 0 || n == 0) return QMM_OK;
+    const int dev = current_device();
+    if (dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    const qmm_weight* reg = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_reg_mu);
+        auto it = g_registered.find(w);
+        if (it != g_registered.end() && it->second->dtype == dt && it->second->n == n && it->second->k == k &&
+            it->second->device == dev)
+            reg = it->second;
+    }
+    const size_t wb = n * row_bytes_of(dt, k);
+    const size_t ws = workspace_for(dt, act_for(native), m, n, k, dev);
+    auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const size_t need = al(m * k * 4) + al(m * n * 4) + (reg ? 0 : al(wb)) + al(ws);
+    // a per-thread scratch so concurrent host calls never share device buffers
+    thread_local std::map<int, Buffer> scratch;
+    Buffer& b = scratch[dev];
+    if (b.bytes < need) {
+        if (b.ptr) cudaFree(b.ptr);
+        b.ptr = nullptr;
+        b.bytes = 0;
+        QMM_CUDA(cudaMalloc(&b.ptr, need));
+        QMM_CUDA(cudaMemset(b.ptr, 0, need));
+        b.bytes = need;
+    }
+    uint8_t* base = static_cast<uint8_t*>(b.ptr);
+    float* xd = reinterpret_cast<float*>(base);
+    float* yd = reinterpret_cast<float*>(base + al(m * k * 4));
+    uint8_t* wd = base + al(m * k * 4) + al(m * n * 4);
+    void* wsd = wd + (reg ? 0 : al(wb));
+    const uint8_t* wuse = reg ? reg->dev : wd;
+    cudaStream_t st = nullptr;
+    QMM_CUDA(cudaMemcpyAsync(xd, x, m * k * 4, cudaMemcpyHostToDevice, st));
+    if (!reg) QMM_CUDA(cudaMemcpyAsync(wd, w, wb, cudaMemcpyHostToDevice, st));
+    rc = run_matmul(dt, act_for(native), xd, wuse, m, k, n, yd, wsd, ws, st);
+    if (rc) return rc;
+    QMM_CUDA(cudaMemcpyAsync(y, yd, m * n * 4, cudaMemcpyDeviceToHost, st));
+    QMM_CUDA(cudaStreamSynchronize(st));
+    return QMM_OK;
+}
+
+int host_quantize(int dt, int variant, const float* x, size_t n, uint8_t* out, float* scales) {
+    if (!x || !out) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (n % QK) return fail(QMM_ERR_BLOCK_ALIGNMENT, "element count not divisible by 32");
+    if (n == 0) return QMM_OK;
+    const size_t nb = n / QK, ob = nb * block_bytes(dt);
+    float* xd = nullptr;
+    uint8_t* od = nullptr;
+    float* sd = nullptr;
+    QMM_CUDA(cudaMalloc(&xd, n * 4));
+    cudaError_t e = cudaMalloc(&od, ob);
+    if (e == cudaSuccess && scales) e = cudaMalloc(&sd, nb * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(xd, x, n * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        if (dt == QMM_Q8_0) e = launch_quantize_q8_0(xd, (int64_t)n, od, sd, variant == 1, nullptr);
+        else if (dt == QMM_Q4_0) e = launch_quantize_q4_0(xd, (int64_t)n, od, nullptr);
+        else e = launch_quantize_q4_1(xd, (int64_t)n, od, nullptr);
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(out, od, ob, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && scales) e = cudaMemcpy(scales, sd, nb * 4, cudaMemcpyDeviceToHost);
+    cudaFree(xd);
+    cudaFree(od);
+    if (sd) cudaFree(sd);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize");
+    return QMM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+QMM_API int qmm_version(void) { return 100; }
+
+QMM_API const char* qmm_status_string(int s) {
+    switch (s) {
+        case QMM_OK: return "ok";
+        case QMM_ERR_BLOCK_ALIGNMENT: return "block alignment";
+        case QMM_ERR_SHAPE_MISMATCH: return "shape mismatch";
+        case QMM_ERR_DTYPE_MISMATCH: return "dtype mismatch";
+        case QMM_ERR_INVALID_DATA: return "invalid data";
+        case QMM_ERR_CUDA: return "cuda error";
+        case QMM_ERR_NCCL: return "nccl error";
+        case QMM_ERR_TIMEOUT: return "timeout";
+        case QMM_ERR_INVALID_INPUT: return "invalid input";
+        case QMM_ERR_NO_DEVICE: return "no device";
+        default: return "unknown status";
+    }
+}
+
+QMM_API const char* qmm_last_error_message(void) { return t_last_error.c_str(); }
+
+QMM_API int qmm_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+QMM_API int qmm_device_error(int device, int* out_error) {
+    if (!out_error) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(QMM_ERR_INVALID_INPUT, "bad device");
+    int* p = device_error_word(device);
+    if (!p) return fail(QMM_ERR_CUDA, "device error word unavailable");
+    QMM_CUDA(cudaDeviceSynchronize());
+    int v = 0;
+    QMM_CUDA(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+    const int zero = 0;
+    QMM_CUDA(cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    *out_error = v;
+    return QMM_OK;
+}
+
+#define QMM_HOST_MATMUL(name, dt, native)                                                                      \
+    QMM_API int name(const float* input_data, size_t input_len, const uint8_t* weight_bytes, size_t weight_len, \
+                     size_t m, size_t in_features, size_t out_features, float* output) {                       \
+        return host_matmul(dt, native, input_data, input_len, weight_bytes, weight_len, m, in_features,       \
+                           out_features, output);                                                              \
+    }
+QMM_HOST_MATMUL(qmm_matmul_f32_q8, QMM_Q8_0, false)
+QMM_HOST_MATMUL(qmm_matmul_f32_q8_v2, QMM_Q8_0, true)
+QMM_HOST_MATMUL(qmm_matmul_f32_q4, QMM_Q4_0, false)
+QMM_HOST_MATMUL(qmm_matmul_f32_q4_native, QMM_Q4_0, true)
+QMM_HOST_MATMUL(qmm_matmul_f32_q4_1, QMM_Q4_1, false)
+QMM_HOST_MATMUL(qmm_matmul_f32_q4_1_native, QMM_Q4_1, true)
+#undef QMM_HOST_MATMUL
+
+QMM_API int qmm_quantize_q8_0(const float* data, size_t n, uint8_t* out) {
+    return host_quantize(QMM_Q8_0, 0, data, n, out, nullptr);
+}
+QMM_API int qmm_quantize_q4_0(const float* data, size_t n, uint8_t* out) {
+    return host_quantize(QMM_Q4_0, 0, data, n, out, nullptr);
+}
+QMM_API int qmm_quantize_q4_1(const float* data, size_t n, uint8_t* out) {
+    return host_quantize(QMM_Q4_1, 0, data, n, out, nullptr);
+}
+QMM_API int qmm_quantize_row_q8_0(const float* input, size_t n, uint8_t* out, float* scales) {
+    if (!scales) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    return host_quantize(QMM_Q8_0, 1, input, n, out, scales);
+}
+
+QMM_API int qmm_dequantize(int dtype, const uint8_t* raw, size_t raw_len, size_t n_elements, float* out) {
+    if (!raw || !out) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (!valid_dtype(dtype)) return fail(QMM_ERR_DTYPE_MISMATCH, "unsupported block type id");
+    if (n_elements % QK) return fail(QMM_ERR_BLOCK_ALIGNMENT, "element count not divisible by 32");
+    const size_t bytes = n_elements / QK * block_bytes(dtype);
+    if (raw_len < bytes) return fail(QMM_ERR_SHAPE_MISMATCH, "raw buffer shorter than the element count needs");
+    if (n_elements == 0) return QMM_OK;
+    uint8_t* wd = nullptr;
+    float* od = nullptr;
+    QMM_CUDA(cudaMalloc(&wd, bytes));
+    cudaError_t e = cudaMalloc(&od, n_elements * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(wd, raw, bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_dequantize(dtype, wd, (int64_t)n_elements, od, nullptr);
+    if (e == cudaSuccess) e = cudaMemcpy(out, od, n_elements * 4, cudaMemcpyDeviceToHost);
+    cudaFree(wd);
+    cudaFree(od);
+    if (e != cudaSuccess) return cuda_fail(e, "dequantize");
+    return QMM_OK;
+}
+
+QMM_API int qmm_register_host_weight(const uint8_t* weight_bytes, size_t weight_len, int dtype, size_t n, size_t k) {
+    if (!weight_bytes) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    const int dev = current_device();
+    if (dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    qmm_weight* w = nullptr;
+    int rc = weight_create_impl(dtype, n, k, weight_bytes, weight_len, dev, false, &w);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(g_reg_mu);
+    auto it = g_registered.find(weight_bytes);
+    if (it != g_registered.end()) qmm_weight_destroy(it->second);
+    g_registered[weight_bytes] = w;
+    return QMM_OK;
+}
+
+QMM_API int qmm_unregister_host_weight(const uint8_t* weight_bytes) {
+    std::lock_guard<std::mutex> lock(g_reg_mu);
+    auto it = g_registered.find(weight_bytes);
+    if (it == g_registered.end()) return fail(QMM_ERR_INVALID_INPUT, "not registered");
+    qmm_weight_destroy(it->second);
+    g_registered.erase(it);
+    return QMM_OK;
+}
+
+QMM_API int qmm_weight_create(int dtype, size_t n, size_t k, const uint8_t* host_bytes, size_t len, int device,
+                              qmm_weight** out) {
+    return weight_create_impl(dtype, n, k, host_bytes, len, device, false, out);
+}
+
+QMM_API int qmm_weight_create_from_device(int dtype, size_t n, size_t k, const uint8_t* dev_bytes, size_t len,
+                                          int device, qmm_weight** out) {
+    return weight_create_impl(dtype, n, k, dev_bytes, len, device, true, out);
+}
+
+QMM_API int qmm_weight_destroy(qmm_weight* w) {
+    if (!w) return QMM_OK;
+    {
+        DeviceGuard guard(w->device);
+        cudaFree(w->dev);
+    }
+    delete w;
+    return QMM_OK;
+}
+
+QMM_API int qmm_weight_info(const qmm_weight* w, int* dtype, size_t* n, size_t* k, const uint8_t** dev_bytes,
+                            int* device) {
+    if (!w) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (dtype) *dtype = w->dtype;
+    if (n) *n = w->n;
+    if (k) *k = w->k;
+    if (dev_bytes) *dev_bytes = w->dev;
+    if (device) *device = w->device;
+    return QMM_OK;
+}
+
+QMM_API size_t qmm_workspace_size(int dtype, int act, size_t m, size_t n, size_t k) {
+    if (!valid_dtype(dtype) || k % QK || k == 0) return 0;
+    const int dev = current_device();
+    if (dev < 0) return 0;
+    return workspace_for(dtype, act, m, n, k, dev);
+}
+
+QMM_API int qmm_reserve_workspace(int device, void* stream, size_t bytes) {
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(QMM_ERR_INVALID_INPUT, "bad device");
+    void* p = nullptr;
+    return get_workspace(device, stream, bytes, &p);
+}
+
+QMM_API int qmm_matmul_dev(int dtype, int act, const float* x_dev, const uint8_t* w_dev, size_t w_len, size_t m,
+                           size_t k, size_t n, float* y_dev, void* workspace_dev, size_t workspace_bytes,
+                           void* stream) {
+    if (act != QMM_ACT_F32 && act != QMM_ACT_Q8_0) return fail(QMM_ERR_INVALID_INPUT, "bad activation mode");
+    int rc = check_shape(dtype, m, k, n, w_len);
+    if (rc) return rc;
+    if (m == 0 || n == 0) return QMM_OK;
+    if (!x_dev || !w_dev || !y_dev || !workspace_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (((uintptr_t)w_dev & 15) || ((uintptr_t)x_dev & 3) || ((uintptr_t)y_dev & 3) || ((uintptr_t)workspace_dev & 255))
+        return fail(QMM_ERR_INVALID_INPUT, "misaligned pointer (w 16 B, x/y 4 B, workspace 256 B)");
+    return run_matmul(dtype, act, x_dev, w_dev, m, k, n, y_dev, workspace_dev, workspace_bytes,
+                      (cudaStream_t)stream);
+}
+
+QMM_API int qmm_linear_forward(const qmm_weight* w, const float* x_dev, size_t m, float* y_dev, int act,
+                               void* stream) {
+    if (!w || !x_dev || !y_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (act != QMM_ACT_F32 && act != QMM_ACT_Q8_0) return fail(QMM_ERR_INVALID_INPUT, "bad activation mode");
+    if (m == 0) return QMM_OK;
+    DeviceGuard guard(w->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    const size_t need = workspace_for(w->dtype, act, m, w->n, w->k, w->device);
+    void* ws = nullptr;
+    int rc = get_workspace(w->device, stream, need, &ws);
+    if (rc) return rc;
+    return run_matmul(w->dtype, act, x_dev, w->dev, m, w->k, w->n, y_dev, ws, need, (cudaStream_t)stream);
+}
+
+QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, size_t m, float* y_host, int act,
+                                    void* stream) {
+    if (!w || !x_host || !y_host) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (act != QMM_ACT_F32 && act != QMM_ACT_Q8_0) return fail(QMM_ERR_INVALID_INPUT, "bad activation mode");
+    if (m == 0) return QMM_OK;
+    DeviceGuard guard(w->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const size_t ws_need = workspace_for(w->dtype, act, m, w->n, w->k, w->device);
+    const size_t io = al(m * w->k * 4) + al(m * w->n * 4);
+    void* ws = nullptr;
+    int rc = get_workspace(w->device, stream, ws_need + io, &ws);
+    if (rc) return rc;
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    float* xd = reinterpret_cast<float*>(base + al(ws_need));
+    float* yd = reinterpret_cast<float*>(base + al(ws_need) + al(m * w->k * 4));
+    cudaStream_t st = (cudaStream_t)stream;
+    QMM_CUDA(cudaMemcpyAsync(xd, x_host, m * w->k * 4, cudaMemcpyHostToDevice, st));
+    rc = run_matmul(w->dtype, act, xd, w->dev, m, w->k, w->n, yd, ws, ws_need, st);
+    if (rc) return rc;
+    QMM_CUDA(cudaMemcpyAsync(y_host, yd, m * w->n * 4, cudaMemcpyDeviceToHost, st));
+    QMM_CUDA(cudaStreamSynchronize(st));
+    return QMM_OK;
+}
+
+QMM_API int qmm_quantize_dev(int dtype, int variant, const float* x_dev, size_t n, uint8_t* out_dev,
+                             float* scales_dev, void* stream) {
+    if (!x_dev || !out_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (!valid_dtype(dtype)) return fail(QMM_ERR_DTYPE_MISMATCH, "unsupported block type id");
+    if (n % QK) return fail(QMM_ERR_BLOCK_ALIGNMENT, "element count not divisible by 32");
+    cudaError_t e;
+    if (dtype == QMM_Q8_0) e = launch_quantize_q8_0(x_dev, (int64_t)n, out_dev, scales_dev, variant == 1, (cudaStream_t)stream);
+    else if (dtype == QMM_Q4_0) e = launch_quantize_q4_0(x_dev, (int64_t)n, out_dev, (cudaStream_t)stream);
+    else e = launch_quantize_q4_1(x_dev, (int64_t)n, out_dev, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize");
+    return QMM_OK;
+}
+
+QMM_API int qmm_dequantize_dev(int dtype, const uint8_t* w_dev, size_t w_len, size_t n_elements, float* out_dev,
+                               void* stream) {
+    if (!w_dev || !out_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (!valid_dtype(dtype)) return fail(QMM_ERR_DTYPE_MISMATCH, "unsupported block type id");
+    if (n_elements % QK) return fail(QMM_ERR_BLOCK_ALIGNMENT, "element count not divisible by 32");
+    if (w_len < n_elements / QK * block_bytes(dtype)) return fail(QMM_ERR_SHAPE_MISMATCH, "buffer too short");
+    cudaError_t e = launch_dequantize(dtype, w_dev, (int64_t)n_elements, out_dev, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dequantize");
+    return QMM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,315 @@
+"""GPU parity of the quantized matmul path against the CPU oracle, through the
+C ABI (libqmm.so). Bars (north star):
+  * dequantised weights and Q8_0 activation blocks: bit-exact;
+  * f32-activation outputs: ||y - ref|| / ||ref|| <= 1e-3 and the per-element
+    bound of conftest.assert_close_rel (measured ~1e-5);
+  * Q8_0-activation ("native" / v2) outputs: bit-exact (integer block dots,
+    per-block terms summed in the reference's block order).
+Shapes: every BASELINE configuration's GEMV shapes plus ragged / tiny /
+split-K / batched edge cases.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import assert_close_rel
+
+pytestmark = pytest.mark.gpu
+
+Q4_0, Q4_1, Q8_0 = 2, 3, 8
+BB = {Q4_0: 18, Q4_1: 20, Q8_0: 34}
+ORACLE_FN = {
+    (Q8_0, 0): "matmul_f32_q8", (Q8_0, 1): "matmul_f32_q8_v2",
+    (Q4_0, 0): "matmul_f32_q4", (Q4_0, 1): "matmul_f32_q4_native",
+    (Q4_1, 0): "matmul_f32_q4_1", (Q4_1, 1): "matmul_f32_q4_1_native",
+}
+
+
+@pytest.fixture(scope="module")
+def torch_cuda(qlib):
+    import torch
+    assert torch.cuda.is_available()
+    torch.cuda.init()
+    return torch
+
+
+def make_weights(oracle, dt, n, k, seed, std=0.02):
+    """Block bytes from the reference's own quantisers (restated in the oracle)."""
+    rng = np.random.default_rng(seed)
+    wf = rng.normal(0.0, std, n * k).astype(np.float32)
+    if dt == Q8_0:
+        return oracle.quantize_q8_0(wf)
+    if dt == Q4_0:
+        return oracle.quantize_q4_0(wf)
+    return oracle.quantize_q4_1(wf)
+
+
+def random_blocks(dt, n, k, seed):
+    """Random but well-formed block bytes (fast for very large matrices):
+    scales ~ the magnitude a N(0, 0.02) block would get."""
+    rng = np.random.default_rng(seed)
+    nb = n * (k // 32)
+    raw = rng.integers(0, 256, size=nb * BB[dt], dtype=np.uint8).reshape(nb, BB[dt])
+    d = (rng.uniform(0.5, 1.5, nb) * (0.06 / (127 if dt == Q8_0 else 8))).astype(np.float16).view(np.uint8)
+    raw[:, 0:2] = d.reshape(nb, 2)
+    if dt == Q4_1:
+        mn = (-rng.uniform(0.03, 0.07, nb)).astype(np.float16).view(np.uint8)
+        raw[:, 2:4] = mn.reshape(nb, 2)
+    return raw.ravel()
+
+
+def gpu_matmul(torch, qlib, dt, act, x, w, m, k, n):
+    xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+    wd = torch.from_numpy(np.ascontiguousarray(w, dtype=np.uint8)).cuda()
+    yd = torch.full((max(m * n, 1),), float("nan"), dtype=torch.float32, device="cuda")
+    ws_bytes = qlib.qmm_workspace_size(dt, act, m, n, k)
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = qlib.qmm_matmul_dev(dt, act, xd.data_ptr(), wd.data_ptr(), wd.numel(), m, k, n, yd.data_ptr(),
+                             ws.data_ptr(), ws.numel(), ctypes.c_void_p(st))
+    assert rc == 0, qlib.qmm_last_error_message()
+    torch.cuda.synchronize()
+    return yd[: m * n].cpu().numpy()
+
+
+def check(oracle, torch, qlib, dt, act, x, w, m, k, n):
+    y = gpu_matmul(torch, qlib, dt, act, x, w, m, k, n)
+    ref = getattr(oracle, ORACLE_FN[(dt, act)])(x, w, m, k, n)
+    if act == 1:
+        np.testing.assert_array_equal(y.view(np.uint32), ref.view(np.uint32),
+                                      err_msg=f"native dt={dt} m={m} k={k} n={n} not bit-exact")
+        return 0.0
+    return assert_close_rel(y, ref, 1e-3)
+
+
+def device_error_clear(qlib):
+    e = ctypes.c_int(-1)
+    assert qlib.qmm_device_error(0, ctypes.byref(e)) == 0
+    return e.value
+
+
+# ---- BASELINE configurations ----------------------------------------------------------------
+
+def test_config1_q4_0_gemv_6912x1152(oracle, torch_cuda, qlib):
+    m, k, n = 1, 1152, 6912
+    w = make_weights(oracle, Q4_0, n, k, seed=0)
+    x = np.random.default_rng(100).normal(0, 1, m * k).astype(np.float32)
+    rel = check(oracle, torch_cuda, qlib, Q4_0, 0, x, w, m, k, n)
+    assert rel < 1e-4, rel  # the design point is ~1e-5; 1e-3 is the contract
+    check(oracle, torch_cuda, qlib, Q4_0, 1, x, w, m, k, n)
+
+
+SWEEP = [(1152, 1024), (1152, 256), (1152, 256), (1024, 1152), (1152, 6912), (1152, 6912), (6912, 1152)]
+
+
+@pytest.mark.parametrize("m", [1, 8])
+@pytest.mark.parametrize("idx", range(len(SWEEP)))
+def test_config2_q8_0_sweep(oracle, torch_cuda, qlib, m, idx):
+    k, n = SWEEP[idx]
+    w = make_weights(oracle, Q8_0, n, k, seed=1 + idx)
+    x = np.random.default_rng(200 + idx).normal(0, 1, m * k).astype(np.float32)
+    check(oracle, torch_cuda, qlib, Q8_0, 0, x, w, m, k, n)
+    check(oracle, torch_cuda, qlib, Q8_0, 1, x, w, m, k, n)
+
+
+@pytest.mark.parametrize("m", [1, 32])
+@pytest.mark.parametrize("shape", [(8192, 28672), (28672, 8192)])
+def test_config5_llama70b_q4_0(oracle, torch_cuda, qlib, m, shape):
+    k, n = shape
+    w = random_blocks(Q4_0, n, k, seed=k + n)
+    x = np.random.default_rng(7).normal(0, 1, m * k).astype(np.float32)
+    check(oracle, torch_cuda, qlib, Q4_0, 0, x, w, m, k, n)
+
+
+def test_config5_lm_head_q8_0_row_subset(oracle, torch_cuda, qlib):
+    """128256 x 8192 Q8_0 (1.1 GB): full GPU matmul, oracle on a random
+    contiguous slice of output rows (rows are independent dot products)."""
+    k, n, m = 8192, 128256, 1
+    w = random_blocks(Q8_0, n, k, seed=5)
+    x = np.random.default_rng(8).normal(0, 1, m * k).astype(np.float32)
+    y = gpu_matmul(torch_cuda, qlib, Q8_0, 0, x, w, m, k, n)
+    rb = (k // 32) * 34
+    for r0 in (0, 64000, n - 3000):
+        ref = oracle.matmul_f32_q8(x, w[r0 * rb:(r0 + 3000) * rb], m, k, 3000)
+        assert_close_rel(y[r0:r0 + 3000], ref)
+
+
+# ---- edge cases ------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("dt", [Q4_0, Q8_0, Q4_1])
+@pytest.mark.parametrize("act", [0, 1])
+@pytest.mark.parametrize("m,k,n", [(1, 32, 1), (1, 32, 7), (3, 64, 17), (5, 96, 33), (2, 160, 16),
+                                   (1, 4096, 5), (7, 2048, 48)])
+def test_small_and_ragged(oracle, torch_cuda, qlib, dt, act, m, k, n):
+    w = make_weights(oracle, dt, n, k, seed=m * 1000 + k + n)
+    x = np.random.default_rng(m + k + n).normal(0, 1, m * k).astype(np.float32)
+    check(oracle, torch_cuda, qlib, dt, act, x, w, m, k, n)
+
+
+@pytest.mark.parametrize("m", [2, 4, 9, 15, 16, 17, 24, 33, 47, 64, 65, 100])
+def test_batched_rows(oracle, torch_cuda, qlib, m):
+    k, n = 1152, 300
+    for dt in (Q4_0, Q8_0):
+        w = make_weights(oracle, dt, n, k, seed=m)
+        x = np.random.default_rng(m).normal(0, 1, m * k).astype(np.float32)
+        check(oracle, torch_cuda, qlib, dt, 0, x, w, m, k, n)
+        check(oracle, torch_cuda, qlib, dt, 1, x, w, m, k, n)
+
+
+@pytest.mark.parametrize("scale", [1e-30, 1e-6, 1e4, 1e30])
+def test_activation_magnitudes(oracle, torch_cuda, qlib, scale):
+    """f16 tensor-core inputs with per-block power-of-two scaling: any finite
+    f32 activation range keeps the 1e-3 bound."""
+    m, k, n = 2, 1024, 64
+    w = make_weights(oracle, Q4_0, n, k, seed=3)
+    x = (np.random.default_rng(4).normal(0, 1, m * k) * scale).astype(np.float32)
+    x[:32] = 0.0  # an all-zero block
+    check(oracle, torch_cuda, qlib, Q4_0, 0, x, w, m, k, n)
+    check(oracle, torch_cuda, qlib, Q4_0, 1, x, w, m, k, n)
+
+
+def test_mixed_block_magnitudes(oracle, torch_cuda, qlib):
+    m, k, n = 3, 2048, 40
+    w = make_weights(oracle, Q8_0, n, k, seed=9)
+    rng = np.random.default_rng(10)
+    x = rng.normal(0, 1, (m, k // 32, 32)) * (10.0 ** rng.uniform(-8, 8, (m, k // 32, 1)))
+    x = x.astype(np.float32).ravel()
+    check(oracle, torch_cuda, qlib, Q8_0, 0, x, w, m, k, n)
+    check(oracle, torch_cuda, qlib, Q8_0, 1, x, w, m, k, n)
+
+
+def test_empty_shapes_are_noops(torch_cuda, qlib):
+    assert gpu_matmul(torch_cuda, qlib, Q4_0, 0, np.zeros(0, np.float32), np.zeros(18, np.uint8), 0, 32, 1).size == 0
+    assert gpu_matmul(torch_cuda, qlib, Q8_0, 0, np.zeros(32, np.float32), np.zeros(0, np.uint8), 1, 32, 0).size == 0
+
+
+def test_deterministic(oracle, torch_cuda, qlib):
+    m, k, n = 4, 6912, 1152  # split-K path
+    w = make_weights(oracle, Q4_0, n, k, seed=12)
+    x = np.random.default_rng(13).normal(0, 1, m * k).astype(np.float32)
+    a = gpu_matmul(torch_cuda, qlib, Q4_0, 0, x, w, m, k, n)
+    b = gpu_matmul(torch_cuda, qlib, Q4_0, 0, x, w, m, k, n)
+    np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_misaligned_weight_pointer_rejected(torch_cuda, qlib):
+    wd = torch_cuda.zeros(1024, dtype=torch_cuda.uint8, device="cuda")
+    xd = torch_cuda.zeros(32, dtype=torch_cuda.float32, device="cuda")
+    yd = torch_cuda.zeros(8, dtype=torch_cuda.float32, device="cuda")
+    ws = torch_cuda.zeros(1 << 16, dtype=torch_cuda.uint8, device="cuda")
+    rc = qlib.qmm_matmul_dev(Q4_0, 0, xd.data_ptr(), wd.data_ptr() + 2, 1000, 1, 32, 8, yd.data_ptr(),
+                             ws.data_ptr(), ws.numel(), None)
+    assert rc == 8
+
+
+# ---- bit-exact building blocks -------------------------------------------------------------
+
+@pytest.mark.parametrize("dt", [Q4_0, Q8_0, Q4_1])
+def test_dequantize_bit_exact(oracle, torch_cuda, qlib, dt):
+    n, k = 257, 1152
+    w = make_weights(oracle, dt, n, k, seed=21)
+    from machinelearning_b200 import kernel
+    got = kernel.to_f32(dt, w, n * k)
+    ref = oracle.to_f32(dt, w, n * k)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+    got = kernel.to_f32(dt, random_blocks(dt, 64, 256, 3), 64 * 256)
+    ref = oracle.to_f32(dt, random_blocks(dt, 64, 256, 3), 64 * 256)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def _quant_inputs(golden):
+    rng = np.random.default_rng(31)
+    parts = [golden["edge__x"], rng.normal(0, 1, 32 * 512).astype(np.float32),
+             (rng.normal(0, 1, 32 * 64) * 10.0 ** rng.integers(-40, 38, 32 * 64)).astype(np.float32),
+             (np.round(rng.normal(0, 4, 32 * 64)) / 2).astype(np.float32),  # exact .5 ties
+             np.array([np.nan, np.inf, -np.inf] + [1.0] * 29, np.float32)]
+    return np.concatenate(parts).astype(np.float32)
+
+
+def test_quantizers_bit_exact(oracle, torch_cuda, qlib, golden):
+    from machinelearning_b200 import kernel
+    x = _quant_inputs(golden)
+    np.testing.assert_array_equal(kernel.quantize_q8_0(x), oracle.quantize_q8_0(x))
+    q, s = kernel.quantize_row_q8_0(x)
+    qo, so = oracle.quantize_row_q8_0(x)
+    np.testing.assert_array_equal(q, qo)
+    np.testing.assert_array_equal(s.view(np.uint32), so.view(np.uint32))
+    np.testing.assert_array_equal(kernel.quantize_q4_0(x), oracle.quantize_q4_0(x))
+    np.testing.assert_array_equal(kernel.quantize_q4_1(x), oracle.quantize_q4_1(x))
+    # the committed golden bytes too
+    e = golden["edge__x"]
+    np.testing.assert_array_equal(kernel.quantize_q8_0(e), golden["edge__q8"])
+    np.testing.assert_array_equal(kernel.quantize_q4_0(e), golden["edge__q4"])
+    np.testing.assert_array_equal(kernel.quantize_q4_1(e), golden["edge__q41"])
+
+
+def test_golden_matmuls(torch_cuda, qlib, golden):
+    kinds = {"q8": (Q8_0, 0), "q8_v2": (Q8_0, 1), "q4": (Q4_0, 0), "q4_native": (Q4_0, 1),
+             "q4_1": (Q4_1, 0), "q4_1_native": (Q4_1, 1)}
+    for c in golden["cases"]:
+        name, dt, kind, m, k, n = str(c).split(":")
+        m, k, n = int(m), int(k), int(n)
+        dt, act = kinds[kind]
+        y = gpu_matmul(torch_cuda, qlib, dt, act, golden[name + "__x"], golden[name + "__w"], m, k, n)
+        if act:
+            np.testing.assert_array_equal(y.view(np.uint32), golden[name + "__y"].view(np.uint32), err_msg=name)
+        else:
+            assert_close_rel(y, golden[name + "__y"])
+
+
+# ---- reference-signature host entry points + Linear -------------------------------------------
+
+def test_host_entry_points(oracle, torch_cuda, qlib):
+    from machinelearning_b200 import kernel
+    m, k, n = 3, 1152, 200
+    x = np.random.default_rng(40).normal(0, 1, m * k).astype(np.float32)
+    for (dt, native), fn in kernel.MATMUL.items():
+        w = make_weights(oracle, dt, n, k, seed=dt)
+        y = fn(x, w, m, k, n)
+        ref = oracle.MATMUL[(dt, native)](x, w, m, k, n)
+        if native:
+            np.testing.assert_array_equal(y.view(np.uint32), ref.view(np.uint32))
+        else:
+            assert_close_rel(y, ref)
+        kernel.register_host_weight(w, dt, n, k)
+        y2 = fn(x, w, m, k, n)
+        kernel.unregister_host_weight(w)
+        np.testing.assert_array_equal(y.view(np.uint32), y2.view(np.uint32))
+
+
+def test_linear_forward(oracle, torch_cuda, qlib):
+    from machinelearning_b200.linear import Linear, QuantWeight
+    torch = torch_cuda
+    k, n = 1024, 96
+    w = make_weights(oracle, Q4_0, n, k, seed=50)
+    lin = Linear(QuantWeight.from_host(Q4_0, n, k, w, device=0),
+                 bias=torch.arange(n, dtype=torch.float32, device="cuda"))
+    x = np.random.default_rng(51).normal(0, 1, (2, 3, k)).astype(np.float32)
+    y = lin(torch.from_numpy(x).cuda())
+    assert tuple(y.shape) == (2, 3, n)
+    ref = oracle.matmul_f32_q4(x, w, 6, k, n).reshape(2, 3, n) + np.arange(n, dtype=np.float32)
+    assert_close_rel(y.cpu().numpy(), ref)
+    lin.set_native_q4_matmul(True)
+    y = lin(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = oracle.matmul_f32_q4_native(x, w, 6, k, n).reshape(2, 3, n) + np.arange(n, dtype=np.float32)
+    np.testing.assert_array_equal(y, ref)
+    lin.weight.close()
+
+
+def test_linear_forward_host_entry(oracle, torch_cuda, qlib):
+    from machinelearning_b200.linear import QuantWeight
+    k, n, m = 6912, 1152, 1
+    w = make_weights(oracle, Q8_0, n, k, seed=60)
+    qw = QuantWeight.from_host(Q8_0, n, k, w)
+    x = np.random.default_rng(61).normal(0, 1, m * k).astype(np.float32)
+    y = np.zeros(m * n, np.float32)
+    assert qlib.qmm_linear_forward_host(qw.handle, x.ctypes.data, m, y.ctypes.data, 0, None) == 0
+    assert_close_rel(y, oracle.matmul_f32_q8(x, w, m, k, n))
+    qw.close()
+
+
+def test_no_device_error_recorded(torch_cuda, qlib):
+    assert device_error_clear(qlib) == 0

@@ -117,6 +117,30 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
+// ---- tiled tensor copy (TMA, 2-D, no multicast) ----------------------------------
+// Box lands densely in shared memory (row pitch = box inner bytes). Rows or
+// columns outside the tensor are zero-filled and still counted as bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tmap, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst_smem)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// ---- 16-byte asynchronous copies (LDGSTS) tracked by an mbarrier --------------------
+__device__ __forceinline__ void cp_async_16(void* dst_smem, const void* src_gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed
+// (the arrival is one of the barrier's expected arrivals).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // ---- programmatic dependent launch ----------------------------------------------
 // wait: block until the preceding grid in the stream has completed and its
 // memory is visible. launch_dependents: allow the next grid to start launching.
@@ -126,27 +150,22 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 
 // ---- shared loads ----------------------------------------------------------------
-__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
+// Plain C++ loads (not asm volatile) so the compiler can schedule them; they
+// stay after an mbarrier wait because the wait's asm clobbers "memory".
+__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 // 4 bytes from a 2-byte-aligned shared address.
-__device__ __forceinline__ uint32_t lds_u32_a2(uint32_t addr) {
-    return __byte_perm(lds_u16(addr), lds_u16(addr + 2), 0x5410);
+__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* p) {
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+    return __byte_perm((uint32_t)q[0], (uint32_t)q[1], 0x5410);
 }
 
 // ---- tensor-core fragments (mma.sync, register operands) ----------------------
+// Not volatile: pure functions of their register operands, free to be
+// interleaved with independent work.
 // D(16x8 f32) = A(16x16 f16, row) * B(16x8 f16, col) + D
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -154,8 +173,7 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
 // D(16x8 s32) = A(16x32 s8, row) * B(32x8 s8, col) + D  (exact integer sums)
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));

@@ -37,6 +37,7 @@ struct GemvPlan {
     int nbu;         // blocks per K split
     int kc;          // blocks per pipeline stage
     int pitch;       // shared-memory bytes per row slot of a stage
+    int loader;      // 0: one 2-D TMA tile per stage (16-byte row pitch); 1: cp.async windows
     int units;       // row groups * ks
     int grid;        // CTAs
     size_t smem;     // dynamic shared memory per CTA

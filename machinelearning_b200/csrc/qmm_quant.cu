@@ -93,14 +93,13 @@ __global__ void quantize_q4_0_kernel(const float* __restrict__ x, int64_t nblock
         const float scale = (amax == 0.0f) ? 0.0f : __fdiv_rn(amax, 8.0f);
         const float inv = (scale == 0.0f) ? 0.0f : __fdiv_rn(1.0f, scale);
         const int q = round_clamp(__fmul_rn(v, inv), -8.0f, 7.0f) + 8;
-        const int q_odd = __shfl_down_sync(0xffffffffu, q, 1);
-        uint8_t* o = out + b * Q4_0_BYTES;
-        if ((lane & 1) == 0) o[2 + (lane >> 1)] = (uint8_t)(((q_odd & 0xf) << 4) | (q & 0xf));
-        if (lane == 0) {
-            const uint16_t h = f32_to_f16_bits_rn(scale);
-            o[0] = (uint8_t)(h & 0xff);
-            o[1] = (uint8_t)(h >> 8);
-        }
+        // lanes 0-1 write the f16 scale, lanes 2-17 one packed byte each
+        const uint32_t h = f32_to_f16_bits_rn(scale);
+        const int j = (lane - 2) & 15;
+        const int qe = __shfl_sync(0xffffffffu, q, 2 * j);
+        const int qo = __shfl_sync(0xffffffffu, q, 2 * j + 1);
+        const uint32_t byte = lane == 0 ? (h & 0xffu) : (lane == 1 ? (h >> 8) : (uint32_t)(((qo & 0xf) << 4) | (qe & 0xf)));
+        if (lane < Q4_0_BYTES) out[b * Q4_0_BYTES + lane] = (uint8_t)byte;
     }
 }
 
@@ -115,16 +114,13 @@ __global__ void quantize_q4_1_kernel(const float* __restrict__ x, int64_t nblock
         const float inv = (d == 0.0f) ? 0.0f : __fdiv_rn(1.0f, d);
         float r = roundf(__fmul_rn(__fsub_rn(v, mn), inv));
         const int q = isnan(r) ? 0 : (int)fminf(fmaxf(r, 0.0f), 15.0f);
-        const int q_odd = __shfl_down_sync(0xffffffffu, q, 1);
-        uint8_t* o = out + b * Q4_1_BYTES;
-        if ((lane & 1) == 0) o[4 + (lane >> 1)] = (uint8_t)(((q_odd & 0xf) << 4) | (q & 0xf));
-        if (lane == 0) {
-            const uint16_t hd = f32_to_f16_bits_rn(d), hm = f32_to_f16_bits_rn(mn);
-            o[0] = (uint8_t)(hd & 0xff);
-            o[1] = (uint8_t)(hd >> 8);
-            o[2] = (uint8_t)(hm & 0xff);
-            o[3] = (uint8_t)(hm >> 8);
-        }
+        // lanes 0-3 write d and m (f16 LE), lanes 4-19 one packed byte each
+        const uint32_t hdm = f32_to_f16_bits_rn(d) | ((uint32_t)f32_to_f16_bits_rn(mn) << 16);
+        const int j = (lane - 4) & 15;
+        const int qe = __shfl_sync(0xffffffffu, q, 2 * j);
+        const int qo = __shfl_sync(0xffffffffu, q, 2 * j + 1);
+        const uint32_t byte = lane < 4 ? ((hdm >> (8 * lane)) & 0xffu) : (uint32_t)(((qo & 0xf) << 4) | (qe & 0xf));
+        if (lane < Q4_1_BYTES) out[b * Q4_1_BYTES + lane] = (uint8_t)byte;
     }
 }
 

@@ -80,6 +80,7 @@ struct Buffer {
 };
 std::mutex g_ws_mu;
 std::map<std::pair<int, void*>, Buffer> g_ws;
+std::map<std::pair<int, void*>, Buffer> g_io;  // host-entry staging (qmm_linear_forward_host)
 
 int get_workspace(int dev, void* stream, size_t need, void** out) {
     std::lock_guard<std::mutex> lock(g_ws_mu);
@@ -485,11 +486,29 @@ QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, si
     const size_t ws_need = workspace_for(w->dtype, act, m, w->n, w->k, w->device);
     const size_t io = al(m * w->k * 4) + al(m * w->n * 4);
     void* ws = nullptr;
-    int rc = get_workspace(w->device, stream, ws_need + io, &ws);
+    int rc = get_workspace(w->device, stream, ws_need, &ws);
     if (rc) return rc;
-    uint8_t* base = static_cast<uint8_t*>(ws);
-    float* xd = reinterpret_cast<float*>(base + al(ws_need));
-    float* yd = reinterpret_cast<float*>(base + al(ws_need) + al(m * w->k * 4));
+    // staging buffers for x/y live apart from the compute workspace, so a
+    // graph captured with qmm_linear_forward on this stream keeps its addresses
+    void* iob = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_ws_mu);
+        Buffer& b = g_io[{w->device, stream}];
+        if (b.bytes < io) {
+            if (b.ptr) {
+                cudaStreamSynchronize((cudaStream_t)stream);
+                cudaFree(b.ptr);
+                b.ptr = nullptr;
+                b.bytes = 0;
+            }
+            QMM_CUDA(cudaMalloc(&b.ptr, io));
+            b.bytes = io;
+        }
+        iob = b.ptr;
+    }
+    uint8_t* base = static_cast<uint8_t*>(iob);
+    float* xd = reinterpret_cast<float*>(base);
+    float* yd = reinterpret_cast<float*>(base + al(m * w->k * 4));
     cudaStream_t st = (cudaStream_t)stream;
     QMM_CUDA(cudaMemcpyAsync(xd, x_host, m * w->k * 4, cudaMemcpyHostToDevice, st));
     rc = run_matmul(w->dtype, act, xd, w->dev, m, w->k, w->n, yd, ws, ws_need, st);

@@ -152,6 +152,21 @@ QMM_API int qmm_matmul_dev(int dtype, int act, const float* x_dev, const uint8_t
                            size_t k, size_t n, float* y_dev, void* workspace_dev, size_t workspace_bytes,
                            void* stream);
 
+/* Allocation-free form of qmm_matmul_dev (no counterpart in the reference, which
+ * has no device code). For callers that may not allocate device memory: a
+ * plugin whose host framework owns the device memory pool, or a serving loop
+ * that cannot take cudaMalloc's implicit device-wide synchronisation. The
+ * workspace is a fixed 4 MiB device array inside the library
+ * (QMM_NOALLOC_SCRATCH_BYTES; held by every device that loads the library until
+ * the process exits); shapes whose workspace does not fit are rejected with
+ * QMM_ERR_INVALID_INPUT. The first call on a device, with that device current,
+ * looks the array's address up (make it before any stream capture). The array
+ * is shared: calls that overlap on the GPU race, so keep them ordered (one
+ * stream, or explicit synchronisation). Arguments as qmm_matmul_dev. */
+#define QMM_NOALLOC_SCRATCH_BYTES (4u << 20)
+QMM_API int qmm_matmul_dev_noalloc(int dtype, int act, const float* x_dev, const uint8_t* w_dev, size_t w_len,
+                                   size_t m, size_t k, size_t n, float* y_dev, void* stream);
+
 /* Device quantisers, bit-identical to the reference's:
  *   variant 0: quantize_q8_0   (unrounded inverse scale), dtype QMM_Q8_0
  *   variant 1: quantize_row_q8_0 (f16-rounded inverse scale), dtype QMM_Q8_0; scales_dev optional

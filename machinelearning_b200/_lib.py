@@ -66,6 +66,7 @@ SIGNATURES = {
     "qmm_reserve_workspace": (_I, [_I, _P, _SZ]),
     "qmm_workspace_size": (_SZ, [_I, _I, _SZ, _SZ, _SZ]),
     "qmm_matmul_dev": (_I, [_I, _I, _P, _P, _SZ, _SZ, _SZ, _SZ, _P, _P, _SZ, _P]),
+    "qmm_matmul_dev_noalloc": (_I, [_I, _I, _P, _P, _SZ, _SZ, _SZ, _SZ, _P, _P]),
     "qmm_quantize_dev": (_I, [_I, _I, _P, _SZ, _P, _P, _P]),
     "qmm_dequantize_dev": (_I, [_I, _P, _SZ, _SZ, _P, _P]),
 }

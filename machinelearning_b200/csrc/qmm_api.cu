@@ -22,6 +22,13 @@ using namespace qmm;
 // Device-side error word (one per device context). Kernels receive its address.
 __device__ int g_qmm_device_error = 0;
 
+// Scratch for qmm_matmul_dev_noalloc: a fixed, file-scope device array, so that
+// entry point never allocates. Every device that loads the library holds these
+// 4 MiB until the process exits. Host code must not use the symbol itself as a
+// device address; qmm_matmul_dev_noalloc looks the address up per device.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) uint8_t g_qmm_noalloc_scratch[kNoAllocScratchBytes];
+
 namespace {
 
 thread_local std::string t_last_error;
@@ -515,6 +522,82 @@ QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, si
     if (rc) return rc;
     QMM_CUDA(cudaMemcpyAsync(y_host, yd, m * w->n * 4, cudaMemcpyDeviceToHost, st));
     QMM_CUDA(cudaStreamSynchronize(st));
+    return QMM_OK;
+}
+
+// Allocation-free matmul: the same kernels as qmm_matmul_dev, with the
+// workspace taken from the library's fixed device array instead of the
+// caller. For callers that may not allocate device memory (a plugin whose
+// host framework owns the device memory pool, or a serving loop that cannot
+// afford cudaMalloc's implicit device-wide synchronisation).
+//  * Set-up: the first call on a device (with that device current) looks up
+//    the array's device address with cudaGetSymbolAddress; make that first
+//    call before any stream capture. Later calls only read the cached address.
+//  * Limit: the plan's workspace must fit in 4 MiB (QMM_NOALLOC_SCRATCH_BYTES);
+//    larger shapes return QMM_ERR_INVALID_INPUT.
+//  * The array is shared by every call in the process and keeps the last
+//    call's contents. The parts that must start at zero (the split-K tickets)
+//    are cleared by each call's first kernel; everything else is overwritten
+//    before it is read. Calls that overlap on the GPU (different streams, or
+//    different host threads without ordering) race on it.
+//  * Calls no cudaMalloc/cudaFree and no heap-allocating routine: no caches,
+//    the tensor map is encoded on the stack each call.
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+int* g_noalloc_err[kNoAllocMaxDevices] = {};
+}  // namespace
+
+QMM_API int qmm_matmul_dev_noalloc(int dtype, int act, const float* x_dev, const uint8_t* w_dev, size_t w_len,
+                                   size_t m, size_t k, size_t n, float* y_dev, void* stream) {
+    if (act != QMM_ACT_F32 && act != QMM_ACT_Q8_0) return fail(QMM_ERR_INVALID_INPUT, "bad activation mode");
+    int rc = check_shape(dtype, m, k, n, w_len);
+    if (rc) return rc;
+    if (m == 0 || n == 0) return QMM_OK;
+    if (!x_dev || !w_dev || !y_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (((uintptr_t)w_dev & 15) || ((uintptr_t)x_dev & 3) || ((uintptr_t)y_dev & 3))
+        return fail(QMM_ERR_INVALID_INPUT, "misaligned pointer (w 16 B, x/y 4 B)");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    if (dev >= kNoAllocMaxDevices) return fail(QMM_ERR_INVALID_INPUT, "device index beyond the no-alloc table");
+    void* scratch = nullptr;
+    int* err = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_addr[dev]) {  // one-time set-up on this device
+            void* p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_qmm_noalloc_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+            void* q = nullptr;
+            e = cudaGetSymbolAddress(&q, g_qmm_device_error);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(error word)");
+            g_noalloc_err[dev] = static_cast<int*>(q);
+            g_noalloc_addr[dev] = p;
+        }
+        scratch = g_noalloc_addr[dev];
+        err = g_noalloc_err[dev];
+    }
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    for (size_t r0 = 0; r0 < m; r0 += kMaxGemvRows) {
+        const size_t rows = (m - r0) < kMaxGemvRows ? (m - r0) : kMaxGemvRows;
+        GemvPlan p;
+        if (!gemv_plan(dtype, act == QMM_ACT_Q8_0, (int)rows, (int)n, (int)k, sms, &p))
+            return fail(QMM_ERR_SHAPE_MISMATCH, "shape not supported");
+        const size_t need = gemv_workspace_bytes(p);
+        if (need > kNoAllocScratchBytes) {
+            char msg[160];
+            snprintf(msg, sizeof msg, "workspace of %zu bytes exceeds the no-alloc scratch limit of %zu bytes", need,
+                     kNoAllocScratchBytes);
+            return fail(QMM_ERR_INVALID_INPUT, msg);
+        }
+        GemvWorkspace w_s;
+        gemv_workspace_carve(p, scratch, &w_s);
+        cudaError_t e = launch_gemv(p, w_dev, x_dev + r0 * k, y_dev + r0 * n, w_s, err, (cudaStream_t)stream,
+                                    /*no_host_alloc=*/true);
+        if (e != cudaSuccess) return cuda_fail(e, "launch_gemv (no-alloc)");
+    }
     return QMM_OK;
 }
 

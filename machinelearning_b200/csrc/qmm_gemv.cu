@@ -545,6 +545,22 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
+// Same tensor map, encoded on the stack with no cache (no heap allocation);
+// used by the allocation-free entry point.
+cudaError_t weight_tensor_map_uncached(const uint8_t* w, const GemvPlan& p, CUtensorMap* out) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return cudaErrorNotSupported;
+    const int R = p.loader == kLoaderTmaPairs ? 2 : 1;
+    const cuuint64_t dims[2] = {(cuuint64_t)(R * p.row_bytes / 4), (cuuint64_t)(p.N / R)};
+    const cuuint64_t strides[1] = {(cuuint64_t)(R * p.row_bytes)};
+    const cuuint32_t box[2] = {(cuuint32_t)(p.pitch / 4), (cuuint32_t)(kRows / R)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // The weights viewed as a [N rows][row_bytes / 4] uint32 tensor with a box of
 // [kc blocks, 32 rows]. Encoded once per (device, pointer, shape, box).
 cudaError_t weight_tensor_map(const uint8_t* w, const GemvPlan& p, CUtensorMap* out) {
@@ -682,7 +698,7 @@ void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws) {
 }
 
 cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvWorkspace& ws,
-                        int* err, cudaStream_t st) {
+                        int* err, cudaStream_t st, bool no_host_alloc) {
     cudaError_t e;
     const int nzero = ws.counters ? (p.N + kRows - 1) / kRows : 0;
     if (p.native) {
@@ -694,11 +710,14 @@ cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, flo
     }
     if (e != cudaSuccess) return e;
     const void* fn = kernel_for(p);
-    e = ensure_dynamic_smem(fn, p.smem);
+    // no_host_alloc: set the attribute and encode the tensor map on every call
+    // instead of going through the (heap-backed) caches
+    e = no_host_alloc ? cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem)
+                      : ensure_dynamic_smem(fn, p.smem);
     if (e != cudaSuccess) return e;
     Args a;
     if (p.loader != kLoaderCpAsync) {
-        e = weight_tensor_map(w, p, &a.tmap);
+        e = no_host_alloc ? weight_tensor_map_uncached(w, p, &a.tmap) : weight_tensor_map(w, p, &a.tmap);
         if (e != cudaSuccess) return e;
     }
     a.loader = p.loader;

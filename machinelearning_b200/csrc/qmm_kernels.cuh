@@ -61,8 +61,9 @@ void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws);
 size_t gemv_counters_offset(const GemvPlan& p);
 size_t gemv_counters_bytes(const GemvPlan& p);
 
+// no_host_alloc: skip the host-side caches (for the allocation-free entry point).
 cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvWorkspace& ws,
-                        int* err, cudaStream_t st);
+                        int* err, cudaStream_t st, bool no_host_alloc = false);
 
 int* device_error_word(int device);
 

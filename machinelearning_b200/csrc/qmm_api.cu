@@ -135,8 +135,10 @@ size_t workspace_for(int dt, int act, size_t m, size_t n, size_t k, int dev) {
 }
 
 // The device matmul: GEMV in chunks of <= 64 activation rows.
+// immutable_w: the weights are library-owned (a qmm_weight, complete before
+// any call), so the GEMV may fetch them before waiting on preceding kernels.
 int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size_t k, size_t n, float* y,
-               void* ws, size_t ws_bytes, cudaStream_t st) {
+               void* ws, size_t ws_bytes, cudaStream_t st, bool immutable_w = false) {
     if (m == 0 || n == 0) return QMM_OK;
     const int dev = current_device();
     if (dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
@@ -147,6 +149,7 @@ int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size
         if (!gemv_plan(dt, act == QMM_ACT_Q8_0, (int)rows, (int)n, (int)k, num_sms(dev), &p))
             return fail(QMM_ERR_SHAPE_MISMATCH, "shape not supported");
         if (gemv_workspace_bytes(p) > ws_bytes) return fail(QMM_ERR_INVALID_INPUT, "workspace too small");
+        p.weights_immutable = immutable_w;
         GemvWorkspace w_s;
         gemv_workspace_carve(p, ws, &w_s);
         cudaError_t e = launch_gemv(p, w, x + r0 * k, y + r0 * n, w_s, err, st);
@@ -204,6 +207,9 @@ int weight_create_impl(int dtype, size_t n, size_t k, const uint8_t* src, size_t
     uint8_t* d = nullptr;
     QMM_CUDA(cudaMalloc(&d, (bytes + 15) & ~size_t(15)));
     cudaError_t e = cudaMemcpy(d, src, bytes, from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    // a device-to-device cudaMemcpy may still be running when it returns: the
+    // handle's bytes must be final before any kernel may read them
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(d);
         return cuda_fail(e, "weight upload");
@@ -257,7 +263,7 @@ int host_matmul(int dt, bool native, const float* x, size_t x_len, const uint8_t
     cudaStream_t st = nullptr;
     QMM_CUDA(cudaMemcpyAsync(xd, x, m * k * 4, cudaMemcpyHostToDevice, st));
     if (!reg) QMM_CUDA(cudaMemcpyAsync(wd, w, wb, cudaMemcpyHostToDevice, st));
-    rc = run_matmul(dt, act_for(native), xd, wuse, m, k, n, yd, wsd, ws, st);
+    rc = run_matmul(dt, act_for(native), xd, wuse, m, k, n, yd, wsd, ws, st, /*immutable_w=*/reg != nullptr);
     if (rc) return rc;
     QMM_CUDA(cudaMemcpyAsync(y, yd, m * n * 4, cudaMemcpyDeviceToHost, st));
     QMM_CUDA(cudaStreamSynchronize(st));
@@ -479,7 +485,8 @@ QMM_API int qmm_linear_forward(const qmm_weight* w, const float* x_dev, size_t m
     void* ws = nullptr;
     int rc = get_workspace(w->device, stream, need, &ws);
     if (rc) return rc;
-    return run_matmul(w->dtype, act, x_dev, w->dev, m, w->k, w->n, y_dev, ws, need, (cudaStream_t)stream);
+    return run_matmul(w->dtype, act, x_dev, w->dev, m, w->k, w->n, y_dev, ws, need, (cudaStream_t)stream,
+                      /*immutable_w=*/true);
 }
 
 QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, size_t m, float* y_host, int act,
@@ -518,7 +525,7 @@ QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, si
     float* yd = reinterpret_cast<float*>(base + al(m * w->k * 4));
     cudaStream_t st = (cudaStream_t)stream;
     QMM_CUDA(cudaMemcpyAsync(xd, x_host, m * w->k * 4, cudaMemcpyHostToDevice, st));
-    rc = run_matmul(w->dtype, act, xd, w->dev, m, w->k, w->n, yd, ws, ws_need, st);
+    rc = run_matmul(w->dtype, act, xd, w->dev, m, w->k, w->n, yd, ws, ws_need, st, /*immutable_w=*/true);
     if (rc) return rc;
     QMM_CUDA(cudaMemcpyAsync(y_host, yd, m * w->n * 4, cudaMemcpyDeviceToHost, st));
     QMM_CUDA(cudaStreamSynchronize(st));

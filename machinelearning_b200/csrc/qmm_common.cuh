@@ -141,6 +141,12 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Orders this thread's earlier generic-proxy shared-memory accesses before its
+// later async-proxy ones (a TMA write into a buffer that was just read).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---- programmatic dependent launch ----------------------------------------------
 // wait: block until the preceding grid in the stream has completed and its
 // memory is visible. launch_dependents: allow the next grid to start launching.

@@ -161,17 +161,21 @@ __global__ void dequantize_kernel(int qt, const uint8_t* __restrict__ w, int64_t
 // which together carry ~22 significant bits. The MMA sees weights biased by
 // the f16 magic-number trick; `corr` is the bias contribution to subtract, and
 // `s` = 2^e restores the scale. Layouts (see qmm_kernels.cuh):
-//   xf  [nb][M][4 t] x {hi: 4 x half2, lo: 4 x half2}    (32 B per record)
-//   xcs [nb][token_pad(M)] x float2 {-corr, s}   (+ xsum [nb][token_pad(M)] for Q4_1)
+//   xf   [nb][M][4 t] x {hi: 4 x half2, lo: 4 x half2}    (32 B per record)
+//   side [nb][token_pad(M)/2 pairs] x 8 words
+//        {-corr0, -corr1, -corr0, -corr1, s0, s1, sx0, sx1}
+//   (the first four are the MMA accumulator's initial value as the GEMV lane
+//   holding tokens (2p, 2p+1) needs it; sx = block sum, Q4_1 only).
 // The element order inside a record is the K permutation the GEMV's A
 // fragments use (K order inside a block is free in a dot product as long as
 // both operands follow it).
 template <int QT>
 __global__ void xprep_f32_kernel(const float* __restrict__ x, int M, int K, int Mpad, __half* __restrict__ xf,
-                                 float2* __restrict__ xcs, float* __restrict__ xsum, unsigned* __restrict__ zero,
-                                 int nzero) {
-    pdl_wait();  // x may be produced by the preceding kernel in the stream
+                                 uint32_t* __restrict__ side, unsigned* __restrict__ zero, int nzero) {
+    // let the next kernel (the GEMV) launch and start streaming its weights;
+    // this kernel writes nothing before the wait below
     pdl_launch_dependents();
+    pdl_wait();  // x may be produced by the preceding kernel in the stream
     const int lane = threadIdx.x & 31;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nzero; i += gridDim.x * blockDim.x) zero[i] = 0u;
     const int nb = K / QK;
@@ -180,11 +184,9 @@ __global__ void xprep_f32_kernel(const float* __restrict__ x, int M, int K, int 
     for (int64_t idx = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); idx < total; idx += warps) {
         const int b = (int)(idx / Mpad);
         const int m = (int)(idx % Mpad);
+        uint32_t* rec8 = side + ((int64_t)b * (Mpad / 2) + (m >> 1)) * 8 + (m & 1);
         if (m >= M) {  // padding tokens: neutral corr/scale
-            if (lane == 0) {
-                xcs[idx] = make_float2(0.0f, 0.0f);
-                if (xsum) xsum[idx] = 0.0f;
-            }
+            if (lane == 0) rec8[0] = rec8[2] = rec8[4] = rec8[6] = 0u;
             continue;
         }
         const float v = x[(int64_t)m * K + (int64_t)b * QK + lane];
@@ -215,23 +217,24 @@ __global__ void xprep_f32_kernel(const float* __restrict__ x, int M, int K, int 
         const float corr = warp_sum(c);
         float sx = 0.0f;
         if (QT == kQ4_1) sx = warp_sum((lane < 16) ? rep : 16.0f * rep);
-        // destination half index inside the 16-half record of thread t
-        int t, idx8;
+        // destination half index inside the 16-half record of thread t: thread t
+        // covers elements 4t..4t+3 (first MMA) and 16+4t..16+4t+3 (second MMA)
+        const int j = lane & 15;
+        const int t = j >> 2;
+        const int r = j & 3;
+        int idx8;
         if (QT == kQ8_0) {
-            t = lane >> 3;
-            idx8 = lane & 7;
+            idx8 = (lane >> 4) * 4 + r;  // byte order: (q0,q1) then (q2,q3)
         } else {
-            const int j = lane & 15;
-            t = j >> 2;
-            const int r = j & 3;
-            idx8 = (lane >> 4) * 4 + (r & 1) * 2 + (r >> 1);
+            idx8 = (lane >> 4) * 4 + (r & 1) * 2 + (r >> 1);  // nibble pairs (n0,n2) then (n1,n3)
         }
         __half* rec = xf + (((int64_t)b * M + m) * 4 + t) * 16;
         rec[idx8] = hi;
         rec[8 + idx8] = lo;
         if (lane == 0) {
-            xcs[idx] = make_float2(-corr, ldexpf(1.0f, e));  // MMA accumulator starts at -corr
-            if (xsum) xsum[idx] = sx;
+            rec8[0] = rec8[2] = __float_as_uint(-corr);  // MMA accumulator starts at -corr
+            rec8[4] = __float_as_uint(ldexpf(1.0f, e));
+            rec8[6] = __float_as_uint(sx);
         }
     }
 }
@@ -240,13 +243,16 @@ __global__ void xprep_f32_kernel(const float* __restrict__ x, int M, int K, int 
 // the reference does before its integer dots -- quantize_q8_0 for Q8_0 weights
 // (matmul_f32_q8_v2, quantize.rs:451) and quantize_row_q8_0 for Q4_0/Q4_1
 // weights (quantize.rs:674-676) -- and laid out for the s8 MMA:
-//   xq  [nb][M][4 t] x 8 bytes {b0, b1}
-//   xsc [nb][token_pad(M)] x int2 {float bits of the f32(f16) scale, sum of q}
+//   xq   [nb][M][4 t] x 8 bytes {b0, b1}
+//   side [nb][token_pad(M)/2 pairs] x 8 words
+//        {c0, c1, c0, c1, xs0, xs1, qsum0, qsum1}
+//   c = -8 * qsum for Q4_0 (sum (n - 8) q = sum n q - 8 sum q), else 0: the s32
+//   MMA accumulator's initial value; xs = f32(f16(scale)) as float bits.
 template <int QT>
 __global__ void xprep_q8_kernel(const float* __restrict__ x, int M, int K, int Mpad, uint8_t* __restrict__ xq,
-                                int2* __restrict__ xsc, unsigned* __restrict__ zero, int nzero) {
+                                uint32_t* __restrict__ side, unsigned* __restrict__ zero, int nzero) {
+    pdl_launch_dependents();  // see xprep_f32_kernel
     pdl_wait();
-    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nzero; i += gridDim.x * blockDim.x) zero[i] = 0u;
     const int nb = K / QK;
@@ -255,24 +261,24 @@ __global__ void xprep_q8_kernel(const float* __restrict__ x, int M, int K, int M
     for (int64_t idx = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); idx < total; idx += warps) {
         const int b = (int)(idx / Mpad);
         const int m = (int)(idx % Mpad);
+        uint32_t* rec8 = side + ((int64_t)b * (Mpad / 2) + (m >> 1)) * 8 + (m & 1);
         if (m >= M) {
-            if (lane == 0) xsc[idx] = make_int2(0, 0);
+            if (lane == 0) rec8[0] = rec8[2] = rec8[4] = rec8[6] = 0u;
             continue;
         }
         const float v = x[(int64_t)m * K + (int64_t)b * QK + lane];
         const Q8Block r = q8_block_lane(v, QT != kQ8_0);
         const int qsum = warp_sum_i(r.q);
-        int t, off;
-        if (QT == kQ8_0) {  // thread t: q[8t .. 8t+7]
-            t = lane >> 3;
-            off = lane & 7;
-        } else {            // thread t: q[4t..4t+3] then q[16+4t..16+4t+3]
-            const int j = lane & 15;
-            t = j >> 2;
-            off = (lane >> 4) * 4 + (j & 3);
-        }
+        // thread t: q[4t..4t+3] then q[16+4t..16+4t+3] (the s8 MMA's k order)
+        const int j = lane & 15;
+        const int t = j >> 2;
+        const int off = (lane >> 4) * 4 + (j & 3);
         xq[(((int64_t)b * M + m) * 4 + t) * 8 + off] = (uint8_t)(int8_t)r.q;
-        if (lane == 0) xsc[idx] = make_int2(__float_as_int(r.d_rt), qsum);
+        if (lane == 0) {
+            rec8[0] = rec8[2] = (uint32_t)(QT == kQ4_0 ? -8 * qsum : 0);
+            rec8[4] = __float_as_uint(r.d_rt);
+            rec8[6] = (uint32_t)qsum;
+        }
     }
 }
 
@@ -328,25 +334,25 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-cudaError_t launch_xprep_f32(int qt, const float* x, int M, int K, __half* xf, float2* xcs, float* xsum,
-                             unsigned* zero, int nzero, cudaStream_t st) {
+cudaError_t launch_xprep_f32(int qt, const float* x, int M, int K, __half* xf, uint32_t* side, unsigned* zero,
+                             int nzero, cudaStream_t st) {
     const int Mpad = token_pad(M);
     const int64_t warps = (int64_t)(K / QK) * Mpad;
     dim3 grid(grid_for_warps(warps, 8)), block(256);
-    void* args[] = {(void*)&x,   (void*)&M,    (void*)&K,    (void*)&Mpad, (void*)&xf,
-                    (void*)&xcs, (void*)&xsum, (void*)&zero, (void*)&nzero};
+    void* args[] = {(void*)&x,    (void*)&M,    (void*)&K,     (void*)&Mpad, (void*)&xf,
+                    (void*)&side, (void*)&zero, (void*)&nzero};
     const void* fn = qt == kQ8_0 ? (const void*)xprep_f32_kernel<kQ8_0>
                                  : (qt == kQ4_0 ? (const void*)xprep_f32_kernel<kQ4_0>
                                                 : (const void*)xprep_f32_kernel<kQ4_1>);
     return launch_pdl(fn, grid, block, 0, st, args);
 }
 
-cudaError_t launch_xprep_q8(int qt, const float* x, int M, int K, uint8_t* xq, int2* xsc, unsigned* zero, int nzero,
-                           cudaStream_t st) {
+cudaError_t launch_xprep_q8(int qt, const float* x, int M, int K, uint8_t* xq, uint32_t* side, unsigned* zero,
+                           int nzero, cudaStream_t st) {
     const int Mpad = token_pad(M);
     const int64_t warps = (int64_t)(K / QK) * Mpad;
     dim3 grid(grid_for_warps(warps, 8)), block(256);
-    void* args[] = {(void*)&x, (void*)&M, (void*)&K, (void*)&Mpad, (void*)&xq, (void*)&xsc, (void*)&zero, (void*)&nzero};
+    void* args[] = {(void*)&x, (void*)&M, (void*)&K, (void*)&Mpad, (void*)&xq, (void*)&side, (void*)&zero, (void*)&nzero};
     const void* fn = qt == kQ8_0 ? (const void*)xprep_q8_kernel<kQ8_0>
                                  : (qt == kQ4_0 ? (const void*)xprep_q8_kernel<kQ4_0>
                                                 : (const void*)xprep_q8_kernel<kQ4_1>);

@@ -217,7 +217,7 @@ def run_ours(args, rank, world, local_rank):
                     else:
                         dist.all_reduce(y)
 
-    launches_per_step = 2 * len(problems) * len(wl["batches"])  # xprep + GEMV per call
+    launches_per_step = None  # counted by the library while one step is captured
     steps_bytes = sum(alg_bytes(b, k, n, dt) for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems)
 
     # ---- CUDA graphs: one per weight copy -------------------------------------------------
@@ -228,8 +228,10 @@ def run_ours(args, rank, world, local_rank):
         stream.synchronize()
         for c in range(copies):
             g = torch.cuda.CUDAGraph()
+            n0 = L.qmm_launch_count()
             with torch.cuda.graph(g, stream=stream):
                 one_step(c)
+            launches_per_step = L.qmm_launch_count() - n0
             graphs.append(g)
     torch.cuda.synchronize(dev)
 
@@ -270,7 +272,7 @@ def run_ours(args, rank, world, local_rank):
     value = steps_bytes * args.steps / (ms / 1e3) / 1e9
 
     # ---- end to end through the C ABI with host buffers ------------------------------------
-    e2e = run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies)
+    e2e = None if args.no_e2e else run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies)
 
     # ---- CPU baseline (rank 0, N=1): the reference path restated in oracle/ -----------------
     cpu = None
@@ -534,6 +536,7 @@ def main(argv=None):
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemma-q8-sweep")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

@@ -63,6 +63,10 @@ QMM_API int qmm_device_count(void);
 /* Reads and clears the device-side error word of `device` (0 = none, 1 = a
  * bounded wait timed out). Synchronises the device. */
 QMM_API int qmm_device_error(int device, int* out_error);
+/* Number of kernel launches this library has issued in this process (stream
+ * captures included), for launch accounting in benchmarks. No counterpart in
+ * the reference (a CPU library). */
+QMM_API unsigned long long qmm_launch_count(void);
 
 /* ------------------------------------------------------------------------
  * Reference-signature host entry points. Host buffers in, host buffers out,

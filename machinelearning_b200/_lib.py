@@ -44,6 +44,7 @@ SIGNATURES = {
     "qmm_last_error_message": (ctypes.c_char_p, []),
     "qmm_device_count": (_I, []),
     "qmm_device_error": (_I, [_I, _P]),
+    "qmm_launch_count": (ctypes.c_ulonglong, []),
     "qmm_matmul_f32_q8": _HOST_MM,
     "qmm_matmul_f32_q8_v2": _HOST_MM,
     "qmm_matmul_f32_q4": _HOST_MM,

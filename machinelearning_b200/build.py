@@ -60,6 +60,7 @@ def _stale(out: str, deps: list[str]) -> bool:
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
     os.makedirs(BUILD_DIR, exist_ok=True)
     objs = []
+    cmds = []
     hdrs = headers()
     for src in sources():
         obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
@@ -70,7 +71,12 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                 cmd += ["-Xptxas", "-v"]
             if verbose:
                 print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+            cmds.append(cmd)
+    # translation units compile independently: run them side by side
+    procs = [subprocess.Popen(c) for c in cmds]
+    failed = [c for c, p in zip(cmds, procs) if p.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     if force or _stale(LIB, objs):
         # static runtime: the library does not depend on whichever libcudart.so
         # the process happens to resolve first (torch ships its own)

@@ -5,6 +5,7 @@
 // codes instead of panics/exceptions, null checks on every pointer, the library
 // frees what it allocates, concurrent calls are allowed (shared state is behind
 // mutexes; per-stream workspaces keep concurrent streams apart).
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -16,6 +17,12 @@
 #include "../../include/qmm.h"
 #include "qmm_common.cuh"
 #include "qmm_kernels.cuh"
+
+namespace qmm {
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+static unsigned long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+}  // namespace qmm
 
 using namespace qmm;
 
@@ -328,6 +335,8 @@ QMM_API int qmm_device_count(void) {
     }
     return n;
 }
+
+QMM_API unsigned long long qmm_launch_count(void) { return qmm::launch_count(); }
 
 QMM_API int qmm_device_error(int device, int* out_error) {
     if (!out_error) return fail(QMM_ERR_INVALID_INPUT, "null pointer");

@@ -1,0 +1,393 @@
+// Resident small-shape GEMV (f32 activations, M <= 16) for sm_100a.
+//
+// Decode GEMVs with a few MB of weights (the Gemma-3-1B projections: 0.3 to
+// 8.5 MB) are latency-bound: HBM delivers their weights in about a
+// microsecond, while a separate activation-prep launch, activation loads at
+// L2 latency and a split-K fix-up through global atomics each cost more. This
+// kernel is one launch per call and keeps everything on chip:
+//   * the grid is made of clusters of `cluster` CTAs; a cluster owns `tw`
+//     consecutive 32-row tiles, and CTA rank r of the cluster owns the K
+//     granules [r*gpc, (r+1)*gpc) of 8 blocks (TMA boxes start 16-byte aligned).
+//   * thread 0 loads the CTA's whole weight share with 2-D TMA boxes onto one
+//     mbarrier -- before the programmatic-dependency wait when the weights are
+//     immutable, so the loads overlap the preceding kernel in the stream.
+//   * after the wait the CTA splits its activation blocks into the f16 hi/lo
+//     records the streaming path's x-prep kernel writes (qmm_quant.cu), here in
+//     shared memory, with one 8-lane group per (block, token).
+//   * each warp takes a contiguous block range of one tile (8 / tw warps per
+//     tile) and writes its partial 32-row x 8-token tile to shared memory; the
+//     CTA sums the warp partials in warp order, and for cluster > 1 the CTAs
+//     sum the cluster's partials in rank order through distributed shared
+//     memory. No global workspace and no atomics: results are deterministic.
+// The per-block arithmetic (dequantisation, MMA, scales) is consume_group()
+// from qmm_gemv_frag.cuh, shared with the streaming kernel.
+#include <cuda.h>
+
+#include "qmm_common.cuh"
+#include "qmm_gemv_frag.cuh"
+#include "qmm_kernels.cuh"
+
+namespace qmm {
+
+namespace {
+
+struct RArgs {
+    CUtensorMap tmap;  // weights as in the streaming kernel (same box)
+    const float* x;
+    float* y;
+    int M, N, K, nb, row_bytes, pitch, cluster, tw, gpc, weights_immutable;
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA of the cluster: release this CTA's shared-memory
+// writes, acquire the others'.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile(
+        "barrier.cluster.arrive.release.aligned;\n\t"
+        "barrier.cluster.wait.acquire.aligned;" ::
+            : "memory");
+}
+// The f32 at the same shared-memory offset as `local` in CTA `rank` of the cluster.
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+    uint32_t ra;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+
+// 2^n as an exact f32 for n in [-127, 127] (2^-127 is subnormal).
+__device__ __forceinline__ float exp2_int(int n) {
+    return n >= -126 ? __int_as_float((n + 127) << 23) : __int_as_float(0x00400000);
+}
+// The exponent E with a = f * 2^E, f in [0.5, 1), for finite a > 0 (the
+// exponent frexpf returns), read from the bits.
+__device__ __forceinline__ int frexp_exponent(float a) {
+    const int bits = __float_as_int(a);
+    const int biased = bits >> 23;
+    if (biased != 0) return biased - 126;
+    return (31 - __clz(bits)) - 148;  // subnormal: highest set mantissa bit
+}
+
+template <int QT, int NT, int LOADER>
+__global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid_constant__ RArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int BB = block_bytes(QT);
+    constexpr int MP = 8 * NT;  // tokens padded to the MMA tiles
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const ResidentLayout L = resident_layout(a.tw, a.gpc, a.pitch, a.M);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
+    const int rank = (int)cluster_ctarank();
+    const int tile0 = (int)cluster_id_x() * a.tw;
+    const int G = (a.nb + kChunk - 1) / kChunk;
+    const int g0 = rank * a.gpc;
+    const int ng = max(0, min(a.gpc, G - g0));           // granules held by this CTA
+    const int kb0 = g0 * kChunk;                          // its first block
+    const int nbc = max(0, min(a.nb - kb0, ng * kChunk));  // its blocks
+    const int ntl = min(a.tw, (a.N + kRows - 1) / kRows - tile0);  // its tiles (>= 1)
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        prefetch_tmap(&a.tmap);
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    // Rows past N and columns past the row end are zero-filled by TMA and
+    // still counted as transaction bytes.
+    auto issue = [&]() {
+        if (threadIdx.x != 0 || ng == 0) return;
+        mbar_arrive_expect_tx(bar, (uint32_t)(ntl * ng * kRows * a.pitch));
+        for (int tl = 0; tl < ntl; ++tl) {
+            const int tile = tile0 + tl;
+            for (int gi = 0; gi < ng; ++gi) {
+                uint8_t* st = smem + L.stages + (uint32_t)(tl * a.gpc + gi) * kRows * a.pitch;
+                const int kb = kb0 + gi * kChunk;
+                if constexpr (LOADER == kLoaderTmaPairs) {
+                    tma_load_2d(st, &a.tmap, kb * BB / 4, tile * (kRows / 2), bar);
+                    tma_load_2d(st + (kRows / 2) * a.pitch, &a.tmap, (a.row_bytes + kb * BB - 8) / 4,
+                                tile * (kRows / 2), bar);
+                } else {
+                    tma_load_2d(st, &a.tmap, kb * BB / 4, tile * kRows, bar);
+                }
+            }
+        }
+    };
+    if (a.weights_immutable) issue();
+    pdl_wait();  // x (and mutable weights) come from preceding work in the stream
+    if (!a.weights_immutable) issue();
+
+    // ---- activation records for blocks [kb0, kb0 + nbc) -----------------------------
+    // Per (block, token): scale by 2^-e so max|x| lands in [2^13, 2^14), split
+    // into hi = f16(x') and lo = f16(x' - hi); corr is the magic-number bias
+    // the MMA adds, s = 2^e, sx = block sum (Q4_1). Layout and element order
+    // as written by xprep_f32_kernel.
+    {
+        uint8_t* xf = smem + L.xf;
+        uint32_t* side = reinterpret_cast<uint32_t*>(smem + L.side);
+        const int npt = MP - a.M;  // padding tokens per block: neutral records
+        for (int i = threadIdx.x; i < nbc * npt; i += kThreads) {
+            const int b = i / npt, m = a.M + i % npt;
+            uint32_t* r8 = side + (b * (MP / 2) + (m >> 1)) * 8 + (m & 1);
+            r8[0] = r8[2] = r8[4] = r8[6] = 0u;
+        }
+        const bool x16 = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+        const int ntask = nbc * a.M;
+        const int gl = lane & 7;         // lane in the 8-lane group: elements 4gl..4gl+3
+        const bool upper = gl >= 4;      // elements 16..31
+        // kPrepUnroll rounds of 32 tasks per pass: their global loads are all
+        // in flight together instead of one L2 round trip per round
+        constexpr int kPrepUnroll = 4;
+        constexpr int kRound = kThreads / 8;
+        for (int base = warp * 4; base < ntask; base += kRound * kPrepUnroll) {  // warp-uniform trip count
+          float vu[kPrepUnroll][4];
+#pragma unroll
+          for (int u = 0; u < kPrepUnroll; ++u) {
+            const int task = base + u * kRound + (lane >> 3);
+            vu[u][0] = vu[u][1] = vu[u][2] = vu[u][3] = 0.0f;
+            if (task < ntask) {
+                const int b = task / a.M, m = task % a.M;
+                const float* src = a.x + (int64_t)m * a.K + (int64_t)(kb0 + b) * QK + 4 * gl;
+                if (x16) {
+                    const float4 q = *reinterpret_cast<const float4*>(src);
+                    vu[u][0] = q.x;
+                    vu[u][1] = q.y;
+                    vu[u][2] = q.z;
+                    vu[u][3] = q.w;
+                } else {
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) vu[u][r] = src[r];
+                }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kPrepUnroll; ++u) {
+            if (base + u * kRound >= ntask) break;  // warp-uniform
+            const int task = base + u * kRound + (lane >> 3);
+            const bool live = task < ntask;
+            const int b = live ? task / a.M : 0;
+            const int m = live ? task % a.M : 0;
+            const float v[4] = {vu[u][0], vu[u][1], vu[u][2], vu[u][3]};
+            float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+            int e = 0;
+            if (am > 0.0f && am <= 3.402823466e38f) e = max(-126, min(127, frexp_exponent(am) - 14));
+            // Q4 formats: high-nibble elements meet weights pre-multiplied by 16
+            // by the magic trick, so their activations are pre-divided by 16.
+            // Multiplying by an exact power of two rounds exactly as ldexpf.
+            const float scale = exp2_int(-e) * ((QT != kQ8_0 && upper) ? 0.0625f : 1.0f);
+            const float coef = QT == kQ8_0 ? 1152.0f : (QT == kQ4_0 ? (upper ? 1152.0f : 1032.0f) : 1024.0f);
+            // record order inside each group of four: Q8_0 (0,1,2,3), Q4 (0,2,1,3)
+            constexpr int P1 = QT == kQ8_0 ? 1 : 2, P2 = QT == kQ8_0 ? 2 : 1;
+            float vv[4];
+            vv[0] = v[0] * scale;
+            vv[1] = v[P1] * scale;
+            vv[2] = v[P2] * scale;
+            vv[3] = v[3] * scale;
+            const __half2 h01 = __floats2half2_rn(vv[0], vv[1]), h23 = __floats2half2_rn(vv[2], vv[3]);
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            const __half2 l01 = __floats2half2_rn(vv[0] - f01.x, vv[1] - f01.y);
+            const __half2 l23 = __floats2half2_rn(vv[2] - f23.x, vv[3] - f23.y);
+            const float2 g01 = __half22float2(l01), g23 = __half22float2(l23);
+            const float rep[4] = {f01.x + g01.x, f01.y + g01.y, f23.x + g23.x, f23.y + g23.y};
+            float corr = coef * rep[0] + coef * rep[1] + coef * rep[2] + coef * rep[3];
+            float sx = 0.0f;
+            if (QT == kQ4_1) sx = (rep[0] + rep[1] + rep[2] + rep[3]) * (upper ? 16.0f : 1.0f);
+            corr += __shfl_xor_sync(0xffffffffu, corr, 1);
+            corr += __shfl_xor_sync(0xffffffffu, corr, 2);
+            corr += __shfl_xor_sync(0xffffffffu, corr, 4);
+            if (QT == kQ4_1) {
+                sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+                sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+                sx += __shfl_xor_sync(0xffffffffu, sx, 4);
+            }
+            if (live) {
+                // thread t's record holds elements 4t..4t+3 then 16+4t..16+4t+3
+                uint8_t* rec = xf + ((uint32_t)(b * a.M + m) * 4 + (gl & 3)) * 32 + (upper ? 8 : 0);
+                *reinterpret_cast<uint2*>(rec) = make_uint2(h2_bits(h01), h2_bits(h23));
+                *reinterpret_cast<uint2*>(rec + 16) = make_uint2(h2_bits(l01), h2_bits(l23));
+                if (gl == 0) {
+                    uint32_t* r8 = side + (b * (MP / 2) + (m >> 1)) * 8 + (m & 1);
+                    r8[0] = r8[2] = __float_as_uint(-corr);  // the MMA accumulator starts at -corr
+                    r8[4] = __float_as_uint(exp2_int(e));
+                    r8[6] = __float_as_uint(sx);
+                }
+            }
+          }
+        }
+    }
+    __syncthreads();
+    bool ok = true;
+    if (ng > 0) {
+        ok = mbar_wait_bounded(bar, 0, a.err);
+        // gave up (error word set): let the copies land before the CTA moves on
+        if (!ok) mbar_wait_bounded(bar, 0, nullptr);
+    }
+
+    // ---- per-warp partial tiles ---------------------------------------------------------
+    const int wpt = kW / a.tw;  // warps per tile
+    const int tl = warp / wpt, sub = warp % wpt;
+    const int g = lane >> 2, t = lane & 3;
+    float acc[2][NT][4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[r][nt][0] = acc[r][nt][1] = acc[r][nt][2] = acc[r][nt][3] = 0.0f;
+    if (ok && tl < ntl) {
+        const int b_begin = nbc * sub / wpt, b_end = nbc * (sub + 1) / wpt;
+        const uint8_t* xfb = smem + L.xf;
+        const uint4* sd = reinterpret_cast<const uint4*>(smem + L.side);
+        const uint8_t* tbase = smem + L.stages + (uint32_t)(tl * a.gpc) * kRows * a.pitch;
+        for (int b = b_begin; b < b_end; ++b) {
+            XFrag xr[NT];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int m = nt * 8 + g;
+                if (m < a.M) {
+                    const uint4* p = reinterpret_cast<const uint4*>(xfb + ((uint32_t)(b * a.M + m) * 4 + t) * 32);
+                    xr[nt].hi = p[0];
+                    xr[nt].lo = p[1];
+                } else {
+                    xr[nt].hi = make_uint4(0, 0, 0, 0);
+                    xr[nt].lo = make_uint4(0, 0, 0, 0);
+                }
+                xr[nt].c4 = sd[(b * (MP / 2) + nt * 4 + t) * 2];
+                xr[nt].s4 = sd[(b * (MP / 2) + nt * 4 + t) * 2 + 1];
+            }
+            const uint8_t* sbase = tbase + (uint32_t)(b >> 3) * kRows * a.pitch;
+            const uint32_t o = (uint32_t)(b & 7) * BB;
+            const uint8_t* r0 = stage_row<LOADER>(sbase, g, a.pitch) + o;
+            const uint8_t* r1 = stage_row<LOADER>(sbase, g + 8, a.pitch) + o;
+            const uint8_t* r2 = stage_row<LOADER>(sbase, g + 16, a.pitch) + o;
+            const uint8_t* r3 = stage_row<LOADER>(sbase, g + 24, a.pitch) + o;
+            // payloads of odd blocks in a 16-byte aligned box are 4-byte aligned
+            // (Q8_0, Q4_0); Q4_1 payloads always are
+            if (QT == kQ4_1 || (b & 1)) {
+                consume_group<QT, NT, false, true>(r0, r1, t, xr, acc[0]);
+                consume_group<QT, NT, false, true>(r2, r3, t, xr, acc[1]);
+            } else {
+                consume_group<QT, NT, false, false>(r0, r1, t, xr, acc[0]);
+                consume_group<QT, NT, false, false>(r2, r3, t, xr, acc[1]);
+            }
+        }
+    }
+    float* part = reinterpret_cast<float*>(smem + L.part);  // [kW][NT][32 rows][8 tokens]
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            float* p0 = part + ((warp * NT + nt) * kRows + 16 * r + g) * 8 + 2 * t;
+            *reinterpret_cast<float2*>(p0) = make_float2(acc[r][nt][0], acc[r][nt][1]);
+            *reinterpret_cast<float2*>(p0 + 64) = make_float2(acc[r][nt][2], acc[r][nt][3]);  // row + 8
+        }
+    }
+    __syncthreads();
+
+    // ---- CTA sums (warp order), then cluster sums (rank order) -------------------------
+    float* cpart = reinterpret_cast<float*>(smem + L.cpart);  // [tw][MP][32 rows]
+    const int nout = ntl * a.M * kRows;  // row fastest: coalesced stores of y
+    for (int o = threadIdx.x; o < nout; o += kThreads) {
+        const int row = o % kRows, m = (o / kRows) % a.M, tl2 = o / (kRows * a.M);
+        float s = 0.0f;
+        for (int q = 0; q < wpt; ++q) s += part[(((tl2 * wpt + q) * NT + (m >> 3)) * kRows + row) * 8 + (m & 7)];
+        if (a.cluster == 1) {
+            const int n = (tile0 + tl2) * kRows + row;
+            if (n < a.N) a.y[(int64_t)m * a.N + n] = s;
+        } else {
+            cpart[(tl2 * MP + m) * kRows + row] = s;
+        }
+    }
+    if (a.cluster > 1) {
+        cluster_sync();
+        for (int o = rank * kThreads + threadIdx.x; o < nout; o += a.cluster * kThreads) {
+            const int row = o % kRows, m = (o / kRows) % a.M, tl2 = o / (kRows * a.M);
+            const float* src = cpart + (tl2 * MP + m) * kRows + row;
+            float s = 0.0f;
+            for (int q = 0; q < a.cluster; ++q) s += ld_cluster_f32(src, (uint32_t)q);
+            const int n = (tile0 + tl2) * kRows + row;
+            if (n < a.N) a.y[(int64_t)m * a.N + n] = s;
+        }
+        cluster_sync();  // no CTA leaves while its partials may still be read
+    }
+}
+
+template <int QT, int LOADER>
+const void* pick_nt(int nt) {
+    return nt == 1 ? (const void*)gemv_resident_kernel<QT, 1, LOADER> : (const void*)gemv_resident_kernel<QT, 2, LOADER>;
+}
+
+template <int QT>
+const void* pick_loader(int loader, int nt) {
+    return loader == kLoaderTmaPairs ? pick_nt<QT, kLoaderTmaPairs>(nt) : pick_nt<QT, kLoaderTma2d>(nt);
+}
+
+const void* resident_kernel_for(const GemvPlan& p) {
+    if (p.qt == kQ8_0) return pick_loader<kQ8_0>(p.loader, p.nt);
+    if (p.qt == kQ4_0) return pick_loader<kQ4_0>(p.loader, p.nt);
+    return pick_loader<kQ4_1>(p.loader, p.nt);
+}
+
+}  // namespace
+
+cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,
+                                 cudaStream_t st, bool no_host_alloc) {
+    if (p.native || p.nt > 2 || p.loader == kLoaderCpAsync) return cudaErrorInvalidValue;
+    const void* fn = resident_kernel_for(p);
+    cudaError_t e = no_host_alloc ? cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem)
+                                  : ensure_dynamic_smem(fn, p.smem);
+    if (e != cudaSuccess) return e;
+    RArgs a;
+    a.tmap = tmap;
+    a.x = x;
+    a.y = y;
+    a.M = p.M;
+    a.N = p.N;
+    a.K = p.K;
+    a.nb = p.nb;
+    a.row_bytes = p.row_bytes;
+    a.pitch = p.pitch;
+    a.cluster = p.cluster;
+    a.tw = p.tw;
+    a.gpc = p.gpc;
+    a.weights_immutable = p.weights_immutable ? 1 : 0;
+    a.err = err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (p.cluster > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)p.cluster;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    void* args[] = {(void*)&a};
+    note_launch();
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace qmm

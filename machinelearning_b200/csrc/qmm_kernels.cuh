@@ -2,6 +2,7 @@
 // kernels. Not installed; the public interface is include/qmm.h.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -25,26 +26,65 @@ cudaError_t launch_xprep_q8(int qt, const float* x, int M, int K, uint8_t* xq, u
                            int nzero, cudaStream_t st);
 cudaError_t launch_pdl_kernel(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args);
 
-// ---- GEMV (qmm_gemv.cu) ---------------------------------------------------------
+// ---- GEMV (qmm_gemv.cu, qmm_gemv_resident.cu) --------------------------------------
+// kGemvStreaming: x-prep kernel, then a persistent GEMV streaming weight tiles
+//                 through per-warp shared-memory rings (any shape, M <= 64).
+// kGemvResident:  one kernel per call for small decode shapes: every CTA loads
+//                 its whole share of the weights into shared memory, prepares
+//                 the activations itself, and K splits are summed on chip
+//                 (warps through shared memory, cluster CTAs through DSMEM).
+enum GemvKind : int { kGemvStreaming = 0, kGemvResident = 1 };
+
 struct GemvPlan {
+    int kind;        // GemvKind
     int qt;          // kQ4_0 / kQ4_1 / kQ8_0
     bool native;     // Q8_0-quantised activations (int8 MMA) instead of f32 activations
     int M, N, K;     // y[M,N] = x[M,K] . W[N,K]^T
     int nb;          // K / 32
     int row_bytes;   // nb * block bytes
     int nt;          // token tiles of 8 (1, 2, 4 or 8)
-    int ks;          // K splits per 32-row tile
-    int nbu;         // blocks per K split
-    int kc;          // blocks per pipeline stage
+    int ks;          // streaming: K splits per 32-row tile
+    int nbu;         // streaming: blocks per K split
+    int kc;          // blocks per pipeline stage / TMA box
     int pitch;       // shared-memory bytes per row slot of a stage
     int loader;      // 0: 2-D TMA tile; 1: cp.async windows; 2: paired-row 2-D TMA tiles
-    int sw;          // shared-memory stages per warp
-    int units;       // tiles * ks
+    int sw;          // streaming: shared-memory stages per warp
+    int units;       // streaming: tiles * ks
+    int cluster;     // resident: CTAs per thread-block cluster (they split K)
+    int tw;          // resident: 32-row tiles per cluster
+    int gpc;         // resident: 8-block granules of K per CTA
     int grid;        // CTAs
     size_t smem;     // dynamic shared memory per CTA
     bool weights_immutable;  // weights are not written by earlier work in the stream:
                              // the GEMV may start fetching them before its dependency wait
 };
+
+// Shared-memory layout of the resident kernel (byte offsets), used by the
+// planner and the kernel alike. M <= 16 tokens, padded to mp = 8 or 16.
+struct ResidentLayout {
+    uint32_t stages, xf, side, part, cpart, bar, total;
+};
+__host__ __device__ inline ResidentLayout resident_layout(int tw, int gpc, int pitch, int M) {
+    const uint32_t mp = M <= 8 ? 8u : 16u;
+    const uint32_t blocks = (uint32_t)gpc * 8u;
+    ResidentLayout L;
+    uint32_t o = 0;
+    L.stages = o;  // [tw][gpc] stages of 32 rows x pitch
+    o += (uint32_t)tw * (uint32_t)gpc * 32u * (uint32_t)pitch;
+    o = (o + 127u) & ~127u;
+    L.xf = o;  // [blocks][M][4] x 32 B activation records
+    o += blocks * (uint32_t)M * 128u;
+    L.side = o;  // [blocks][mp / 2] x 32 B side records
+    o += blocks * (mp / 2u) * 32u;
+    L.part = o;  // [8 warps][mp / 8][32 rows][8 tokens] f32 warp partials
+    o += 8u * mp * 32u * 4u;
+    L.cpart = o;  // [tw][mp][32 rows] f32 CTA partials (read by the cluster)
+    o += (uint32_t)tw * mp * 32u * 4u;
+    L.bar = o;  // one mbarrier
+    o += 16u;
+    L.total = o;
+    return L;
+}
 
 // Fills a plan for the given problem on a device with `num_sms` SMs. Returns
 // false if the shape is not handled by the GEMV kernel (M > 64).
@@ -65,6 +105,17 @@ void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws);
 cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvWorkspace& ws,
                         int* err, cudaStream_t st, bool no_host_alloc = false);
 
+// The resident kernel (launch_gemv dispatches to it for kGemvResident plans).
+cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,
+                                 cudaStream_t st, bool no_host_alloc);
+
+// Opts a kernel in to `bytes` of dynamic shared memory on the current device
+// (cached per device and kernel).
+cudaError_t ensure_dynamic_smem(const void* fn, size_t bytes);
+
 int* device_error_word(int device);
+
+// Launch accounting (qmm_launch_count): every launch site calls note_launch().
+void note_launch();
 
 }  // namespace qmm

@@ -298,18 +298,21 @@ cudaError_t launch_quantize_q8_0(const float* x, int64_t n, uint8_t* out, float*
     const int64_t nb = n / QK;
     if (nb == 0) return cudaSuccess;
     quantize_q8_0_kernel<<<grid_for_warps(nb, 8), 256, 0, st>>>(x, nb, out, scales, rounded_inv ? 1 : 0);
+    note_launch();
     return cudaGetLastError();
 }
 cudaError_t launch_quantize_q4_0(const float* x, int64_t n, uint8_t* out, cudaStream_t st) {
     const int64_t nb = n / QK;
     if (nb == 0) return cudaSuccess;
     quantize_q4_0_kernel<<<grid_for_warps(nb, 8), 256, 0, st>>>(x, nb, out);
+    note_launch();
     return cudaGetLastError();
 }
 cudaError_t launch_quantize_q4_1(const float* x, int64_t n, uint8_t* out, cudaStream_t st) {
     const int64_t nb = n / QK;
     if (nb == 0) return cudaSuccess;
     quantize_q4_1_kernel<<<grid_for_warps(nb, 8), 256, 0, st>>>(x, nb, out);
+    note_launch();
     return cudaGetLastError();
 }
 cudaError_t launch_dequantize(int qt, const uint8_t* w, int64_t n, float* out, cudaStream_t st) {
@@ -317,6 +320,7 @@ cudaError_t launch_dequantize(int qt, const uint8_t* w, int64_t n, float* out, c
     int64_t g = (n + 255) / 256;
     if (g > 148 * 32) g = 148 * 32;
     dequantize_kernel<<<(int)g, 256, 0, st>>>(qt, w, n, out);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -331,6 +335,7 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    note_launch();
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

@@ -158,6 +158,58 @@ def test_small_and_ragged(oracle, torch_cuda, qlib, dt, act, m, k, n):
     check(oracle, torch_cuda, qlib, dt, act, x, w, m, k, n)
 
 
+# Shapes that reach the resident small-shape kernel (f32 activations, M <= 16,
+# row pitch 0 or 8 mod 16) in each of its variants: 2-D and paired-row TMA
+# boxes, one or two 8-token tiles, clusters of 1, 2, 4 and 8 CTAs splitting K,
+# 1 to 4 tiles per cluster, partial last K granules (36, 44, 132 blocks) and
+# ragged last tiles. The last shape (odd N, paired pitch) falls back to the
+# streaming kernel.
+RESIDENT = [
+    (Q8_0, 1, 1152, 1000),   # pairs, cluster 4, ragged tile
+    (Q8_0, 13, 1152, 256),   # pairs, 2 token tiles
+    (Q8_0, 16, 6912, 1152),  # 2-D, cluster 8, 2 tiles per cluster
+    (Q8_0, 3, 2048, 96),     # 2-D, cluster 8, one granule per CTA
+    (Q8_0, 1, 1408, 2048),   # pairs, cluster 2, partial granule
+    (Q8_0, 4, 6912, 1152),   # 2-D, cluster 4
+    (Q4_0, 9, 4224, 200),    # pairs, 2 token tiles, cluster 8, partial granule
+    (Q4_0, 2, 8192, 512),    # 2-D, cluster 8
+    (Q4_0, 12, 2048, 2048),  # 2-D, 4 tiles per cluster
+    (Q4_0, 1, 512, 32),      # single CTA
+    (Q4_1, 1, 1152, 330),    # 2-D (20-byte blocks), no cluster, ragged tile
+    (Q4_1, 16, 384, 64),     # 2 token tiles
+    (Q8_0, 1, 1152, 999),    # odd N: streaming fallback
+]
+
+
+@pytest.mark.parametrize("case", range(len(RESIDENT)))
+def test_resident_kernel_variants(oracle, torch_cuda, qlib, case):
+    dt, m, k, n = RESIDENT[case]
+    w = make_weights(oracle, dt, n, k, seed=900 + case)
+    x = np.random.default_rng(950 + case).normal(0, 1, m * k).astype(np.float32)
+    check(oracle, torch_cuda, qlib, dt, 0, x, w, m, k, n)
+    check(oracle, torch_cuda, qlib, dt, 1, x, w, m, k, n)
+
+
+def test_resident_kernel_unaligned_activations(oracle, torch_cuda, qlib):
+    """x only 4-byte aligned: the in-kernel activation prep uses scalar loads."""
+    torch = torch_cuda
+    m, k, n = 3, 1152, 512
+    w = make_weights(oracle, Q8_0, n, k, seed=31)
+    x = np.random.default_rng(32).normal(0, 1, m * k).astype(np.float32)
+    ref = oracle.matmul_f32_q8(x, w, m, k, n)
+    xbuf = torch.zeros(m * k + 4, dtype=torch.float32, device="cuda")
+    xbuf[1:1 + m * k] = torch.from_numpy(x).cuda()
+    wd = torch.from_numpy(w).cuda()
+    yd = torch.full((m * n,), float("nan"), dtype=torch.float32, device="cuda")
+    ws = torch.zeros(max(qlib.qmm_workspace_size(Q8_0, 0, m, n, k), 256), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = qlib.qmm_matmul_dev(Q8_0, 0, xbuf.data_ptr() + 4, wd.data_ptr(), wd.numel(), m, k, n, yd.data_ptr(),
+                             ws.data_ptr(), ws.numel(), ctypes.c_void_p(st))
+    assert rc == 0, qlib.qmm_last_error_message()
+    torch.cuda.synchronize()
+    assert_close_rel(yd.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("m", [2, 4, 9, 15, 16, 17, 24, 33, 47, 64, 65, 100])
 def test_batched_rows(oracle, torch_cuda, qlib, m):
     k, n = 1152, 300

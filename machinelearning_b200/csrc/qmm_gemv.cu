@@ -444,11 +444,15 @@ cudaError_t weight_tensor_map(const uint8_t* w, const GemvPlan& p, CUtensorMap* 
 bool bank_friendly(int pitch_bytes) { return ((pitch_bytes / 4) & 7) == 4; }
 
 // Resident-kernel configuration: clusters of C CTAs splitting K (C a power of
-// two, at most 8), tw 32-row tiles per cluster, one wave of at most one CTA
-// per SM, shared memory within kResidentSmemMax. Among those, the smallest
-// estimated latency: blocks per warp (serial MMA chains), the cluster
-// exchange, the CTA's weight bytes at a per-SM share of HBM bandwidth and the
-// activation-prep rounds. The constants are rough nanosecond estimates.
+// two, at most 8), tw 32-row tiles per cluster, shared memory within
+// kResidentSmemMax, and a grid the device can hold in one wave (the runtime's
+// occupancy answer: at most one CTA per SM when it cannot say). Among those,
+// the smallest estimated latency in nanoseconds, from B200 measurements of
+// the kernel's phases: ~110 per block per warp (dependent MMA chains; x1.6
+// for two token tiles), ~1500 per activation-prep pass (a load round trip
+// plus a dependent chain), ~1200 for the cluster exchange (two cluster
+// barriers and the DSMEM sums), and the CTA's weight bytes at ~60 B/ns (the
+// part of the weight fetch the dependency wait does not hide).
 constexpr size_t kResidentSmemMax = 200 * 1024;
 
 bool resident_plan(GemvPlan& q, int num_sms) {
@@ -462,14 +466,16 @@ bool resident_plan(GemvPlan& q, int num_sms) {
         const int nbc = q.nb < gpc * kChunk ? q.nb : gpc * kChunk;
         for (int tw = 1; tw <= kW; tw *= 2) {
             const long clusters = (T + tw - 1) / tw;
-            if (clusters * C > num_sms) continue;
             const size_t smem = resident_layout(tw, gpc, q.pitch, q.M).total;
             if (smem > kResidentSmemMax) continue;
+            const int cap = resident_capacity(q.qt, q.loader, q.nt, C, smem);
+            if (clusters > (cap > 0 ? (long)cap : (long)(num_sms / C))) continue;
             const int wpt = kW / tw;
             const int bpw = (nbc + wpt - 1) / wpt;
             const double wbytes = (double)tw * gpc * kRows * q.pitch;
-            const int prep_rounds = (nbc * q.M + 31) / 32;
-            const double cost = bpw * 60.0 * q.nt + (C > 1 ? 500.0 : 0.0) + wbytes / 60.0 + prep_rounds * 40.0;
+            const int passes = (nbc * q.M + 32 * kResidentPrepUnroll - 1) / (32 * kResidentPrepUnroll);
+            const double cost =
+                bpw * 110.0 * (q.nt > 1 ? 1.6 : 1.0) + passes * 1500.0 + (C > 1 ? 1200.0 : 0.0) + wbytes / 60.0;
             if (!found || cost < best) {
                 found = true;
                 best = cost;

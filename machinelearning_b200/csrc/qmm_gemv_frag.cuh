@@ -70,7 +70,10 @@ __device__ __forceinline__ uint32_t ld_word(const uint8_t* p) {
 // Lane t covers payload words t and t+4 of each row (elements 4t..4t+3 and
 // 16+4t..16+4t+3 for Q8_0; nibble bytes 4t..4t+3 for Q4): per shared load the
 // 8 rows x 4 words of a warp fall in distinct banks (row pitch = 4 mod 32 words).
-template <int QT, int NT, bool NATIVE, bool AL>
+// SPLIT (f32 mode): the hi and lo halves accumulate in two independent chains
+// of two MMAs that are added at the end, instead of one chain of four -- half
+// the dependent latency, for latency-bound callers.
+template <int QT, int NT, bool NATIVE, bool AL, bool SPLIT = false>
 __device__ __forceinline__ void consume_group(const uint8_t* r0, const uint8_t* r1, int t, const XFrag (&x)[NT],
                                               float (&acc)[NT][4]) {
     const float d0 = f16_bits_to_f32((uint16_t)lds_u16(r0));
@@ -116,10 +119,21 @@ __device__ __forceinline__ void consume_group(const uint8_t* r0, const uint8_t* 
             const float c0[4] = {__uint_as_float(x[nt].c4.x), __uint_as_float(x[nt].c4.y),
                                  __uint_as_float(x[nt].c4.z), __uint_as_float(x[nt].c4.w)};
             float c[4], e[4], f[4], h[4];
-            mma_f16_c(c, A0, x[nt].hi.x, x[nt].hi.y, c0);
-            mma_f16_c(e, A1, x[nt].hi.z, x[nt].hi.w, c);
-            mma_f16_c(f, A0, x[nt].lo.x, x[nt].lo.y, e);
-            mma_f16_c(h, A1, x[nt].lo.z, x[nt].lo.w, f);
+            if constexpr (SPLIT) {
+                const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                float q[4];
+                mma_f16_c(c, A0, x[nt].hi.x, x[nt].hi.y, c0);
+                mma_f16_c(f, A0, x[nt].lo.x, x[nt].lo.y, z);
+                mma_f16_c(e, A1, x[nt].hi.z, x[nt].hi.w, c);
+                mma_f16_c(q, A1, x[nt].lo.z, x[nt].lo.w, f);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) h[i] = e[i] + q[i];
+            } else {
+                mma_f16_c(c, A0, x[nt].hi.x, x[nt].hi.y, c0);
+                mma_f16_c(e, A1, x[nt].hi.z, x[nt].hi.w, c);
+                mma_f16_c(f, A0, x[nt].lo.x, x[nt].lo.y, e);
+                mma_f16_c(h, A1, x[nt].lo.z, x[nt].lo.w, f);
+            }
             const float s0 = __uint_as_float(x[nt].s4.x), s1 = __uint_as_float(x[nt].s4.y);
             if constexpr (QT == kQ4_1) {
                 const float sx0 = __uint_as_float(x[nt].s4.z), sx1 = __uint_as_float(x[nt].s4.w);

@@ -23,6 +23,9 @@
 // from qmm_gemv_frag.cuh, shared with the streaming kernel.
 #include <cuda.h>
 
+#include <mutex>
+#include <type_traits>
+
 #include "qmm_common.cuh"
 #include "qmm_gemv_frag.cuh"
 #include "qmm_kernels.cuh"
@@ -135,6 +138,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
     // into hi = f16(x') and lo = f16(x' - hi); corr is the magic-number bias
     // the MMA adds, s = 2^e, sx = block sum (Q4_1). Layout and element order
     // as written by xprep_f32_kernel.
+    const uint32_t lo_plane = (uint32_t)a.gpc * kChunk * a.M * 64;  // bytes from the hi to the lo plane
     {
         uint8_t* xf = smem + L.xf;
         uint32_t* side = reinterpret_cast<uint32_t*>(smem + L.side);
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
         const bool upper = gl >= 4;      // elements 16..31
         // kPrepUnroll rounds of 32 tasks per pass: their global loads are all
         // in flight together instead of one L2 round trip per round
-        constexpr int kPrepUnroll = 4;
+        constexpr int kPrepUnroll = kResidentPrepUnroll;
         constexpr int kRound = kThreads / 8;
         for (int base = warp * 4; base < ntask; base += kRound * kPrepUnroll) {  // warp-uniform trip count
           float vu[kPrepUnroll][4];
@@ -217,10 +221,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
                 sx += __shfl_xor_sync(0xffffffffu, sx, 4);
             }
             if (live) {
-                // thread t's record holds elements 4t..4t+3 then 16+4t..16+4t+3
-                uint8_t* rec = xf + ((uint32_t)(b * a.M + m) * 4 + (gl & 3)) * 32 + (upper ? 8 : 0);
+                // thread t's 16-byte record holds elements 4t..4t+3 then
+                // 16+4t..16+4t+3, in the hi plane and in the lo plane
+                uint8_t* rec = xf + ((uint32_t)(b * a.M + m) * 4 + (gl & 3)) * 16 + (upper ? 8 : 0);
                 *reinterpret_cast<uint2*>(rec) = make_uint2(h2_bits(h01), h2_bits(h23));
-                *reinterpret_cast<uint2*>(rec + 16) = make_uint2(h2_bits(l01), h2_bits(l23));
+                *reinterpret_cast<uint2*>(rec + lo_plane) = make_uint2(h2_bits(l01), h2_bits(l23));
                 if (gl == 0) {
                     uint32_t* r8 = side + (b * (MP / 2) + (m >> 1)) * 8 + (m & 1);
                     r8[0] = r8[2] = __float_as_uint(-corr);  // the MMA accumulator starts at -corr
@@ -253,15 +258,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
         const uint8_t* xfb = smem + L.xf;
         const uint4* sd = reinterpret_cast<const uint4*>(smem + L.side);
         const uint8_t* tbase = smem + L.stages + (uint32_t)(tl * a.gpc) * kRows * a.pitch;
-        for (int b = b_begin; b < b_end; ++b) {
+        // one block: activation fragments from the hi/lo planes (16 bytes per
+        // lane, consecutive lanes consecutive records: no bank conflicts), then
+        // both 16-row groups with the short MMA chains
+        auto block = [&](int b, auto aligned) {
+            constexpr bool AL = decltype(aligned)::value;
             XFrag xr[NT];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const int m = nt * 8 + g;
                 if (m < a.M) {
-                    const uint4* p = reinterpret_cast<const uint4*>(xfb + ((uint32_t)(b * a.M + m) * 4 + t) * 32);
-                    xr[nt].hi = p[0];
-                    xr[nt].lo = p[1];
+                    const uint8_t* p = xfb + ((uint32_t)(b * a.M + m) * 4 + t) * 16;
+                    xr[nt].hi = *reinterpret_cast<const uint4*>(p);
+                    xr[nt].lo = *reinterpret_cast<const uint4*>(p + lo_plane);
                 } else {
                     xr[nt].hi = make_uint4(0, 0, 0, 0);
                     xr[nt].lo = make_uint4(0, 0, 0, 0);
@@ -271,20 +280,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
             }
             const uint8_t* sbase = tbase + (uint32_t)(b >> 3) * kRows * a.pitch;
             const uint32_t o = (uint32_t)(b & 7) * BB;
-            const uint8_t* r0 = stage_row<LOADER>(sbase, g, a.pitch) + o;
-            const uint8_t* r1 = stage_row<LOADER>(sbase, g + 8, a.pitch) + o;
-            const uint8_t* r2 = stage_row<LOADER>(sbase, g + 16, a.pitch) + o;
-            const uint8_t* r3 = stage_row<LOADER>(sbase, g + 24, a.pitch) + o;
-            // payloads of odd blocks in a 16-byte aligned box are 4-byte aligned
-            // (Q8_0, Q4_0); Q4_1 payloads always are
-            if (QT == kQ4_1 || (b & 1)) {
-                consume_group<QT, NT, false, true>(r0, r1, t, xr, acc[0]);
-                consume_group<QT, NT, false, true>(r2, r3, t, xr, acc[1]);
-            } else {
-                consume_group<QT, NT, false, false>(r0, r1, t, xr, acc[0]);
-                consume_group<QT, NT, false, false>(r2, r3, t, xr, acc[1]);
-            }
+            consume_group<QT, NT, false, AL, true>(stage_row<LOADER>(sbase, g, a.pitch) + o,
+                                                   stage_row<LOADER>(sbase, g + 8, a.pitch) + o, t, xr, acc[0]);
+            consume_group<QT, NT, false, AL, true>(stage_row<LOADER>(sbase, g + 16, a.pitch) + o,
+                                                   stage_row<LOADER>(sbase, g + 24, a.pitch) + o, t, xr, acc[1]);
+        };
+        // payloads of odd blocks in a 16-byte aligned box are 4-byte aligned
+        // (Q8_0, Q4_0); Q4_1 payloads always are. Blocks go in (even, odd)
+        // pairs so both alignments are static and the two blocks interleave.
+        using EvenAl = std::integral_constant<bool, QT == kQ4_1>;
+        using OddAl = std::true_type;
+        int b = b_begin;
+        if (b < b_end && (b & 1)) block(b++, OddAl{});
+        for (; b + 1 < b_end; b += 2) {
+            block(b, EvenAl{});
+            block(b + 1, OddAl{});
         }
+        if (b < b_end) block(b, EvenAl{});
     }
     float* part = reinterpret_cast<float*>(smem + L.part);  // [kW][NT][32 rows][8 tokens]
 #pragma unroll
@@ -343,6 +355,56 @@ const void* resident_kernel_for(const GemvPlan& p) {
 }
 
 }  // namespace
+
+int resident_capacity(int qt, int loader, int nt, int cluster, size_t smem) {
+    GemvPlan p = {};
+    p.qt = qt;
+    p.loader = loader;
+    p.nt = nt;
+    const void* fn = resident_kernel_for(p);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    struct Entry {
+        int dev;
+        const void* fn;
+        int cluster;
+        size_t smem;
+        int cap;
+    };
+    static std::mutex mu;
+    static Entry cache[256];
+    static int used = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i) {
+        const Entry& e = cache[i];
+        if (e.dev == dev && e.fn == fn && e.cluster == cluster && e.smem == smem) return e.cap;
+    }
+    int cap = 0;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess) {
+        if (cluster == 1) {
+            int per_sm = 0, sms = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) == cudaSuccess &&
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+                cap = per_sm * sms;
+        } else {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(cluster * 32);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)cluster;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&cap, fn, &cfg) != cudaSuccess) cap = 0;
+        }
+    }
+    cudaGetLastError();  // a failed query must not surface as the next launch's error
+    if (used < 256) cache[used++] = Entry{dev, fn, cluster, smem, cap};
+    return cap;
+}
 
 cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,
                                  cudaStream_t st, bool no_host_alloc) {

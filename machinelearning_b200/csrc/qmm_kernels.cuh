@@ -72,7 +72,7 @@ __host__ __device__ inline ResidentLayout resident_layout(int tw, int gpc, int p
     L.stages = o;  // [tw][gpc] stages of 32 rows x pitch
     o += (uint32_t)tw * (uint32_t)gpc * 32u * (uint32_t)pitch;
     o = (o + 127u) & ~127u;
-    L.xf = o;  // [blocks][M][4] x 32 B activation records
+    L.xf = o;  // hi plane [blocks][M][4] x 16 B, then the lo plane
     o += blocks * (uint32_t)M * 128u;
     L.side = o;  // [blocks][mp / 2] x 32 B side records
     o += blocks * (mp / 2u) * 32u;
@@ -108,6 +108,16 @@ cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, flo
 // The resident kernel (launch_gemv dispatches to it for kGemvResident plans).
 cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,
                                  cudaStream_t st, bool no_host_alloc);
+
+// Activation-prep tasks ((block, token) pairs) a resident CTA handles per pass:
+// 32 eight-lane groups x this many rounds, loads of a pass in flight together.
+constexpr int kResidentPrepUnroll = 8;
+
+// How many resident-kernel clusters of `cluster` CTAs (CTAs, for cluster 1)
+// with `smem` bytes of shared memory can be resident on the current device at
+// once; 0 if the runtime cannot say. Cached per (device, kernel, cluster,
+// smem) in a fixed table (no heap use).
+int resident_capacity(int qt, int loader, int nt, int cluster, size_t smem);
 
 // Opts a kernel in to `bytes` of dynamic shared memory on the current device
 // (cached per device and kernel).

@@ -1,7 +1,7 @@
 """Benchmark of the quantized-matmul hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemma-q8-sweep|q4-gemv|llama70b]
+                    [--workload gemma-q8-sweep|q4-gemv|llama70b|llama70b-gate]
 
 Workloads (synthetic, seeded, weights ~N(0, 0.02)
 quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
@@ -15,6 +15,14 @@ quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
       copies rotated (287 MB > L2).
   llama70b: Q4_0 gate/up 8192->28672, down 28672->8192, Q8_0
       lm_head 8192->128256, batch 1 and 32 (1.5 GB of weights per batch).
+  llama70b-gate (one projection of configs[4]): Q4_0 8192->28672, batch 1,
+      two weight copies (264 MB > L2); the small case for streaming-kernel
+      profiles.
+
+Small decode shapes (all of gemma-q8-sweep and q4-gemv) run as one resident
+GEMV launch per call; larger ones as an activation-prep launch plus the
+streaming GEMV. gpu_launches is counted by the library while one step is
+captured.
 
 Metric: the reference's own bandwidth formula (quantize.rs:399-404),
     GB/s = sum over GEMVs of (M*K*4 + N*(K/32)*block_bytes + M*N*4) / time.
@@ -59,6 +67,9 @@ WORKLOADS = {
         projections=[("gate", 8192, 28672, Q4_0, "col"), ("up", 8192, 28672, Q4_0, "col"),
                      ("down", 28672, 8192, Q4_0, "row"), ("lm_head", 8192, 128256, Q8_0, "col")],
         batches=[1, 32], copies=1, model="Llama-3-70B layer set"),
+    "llama70b-gate": dict(
+        config_index=4, projections=[("gate", 8192, 28672, Q4_0, "col")], batches=[1], copies=2,
+        model="Llama-3-70B FFN gate, Q4_0"),
 }
 
 
@@ -161,7 +172,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     stream = torch.cuda.Stream(dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
-    copies = wl["copies"]
+    copies = args.copies or wl["copies"]
 
     # ---- weights: this rank's shard of every projection, `copies` layers --------------
     # column-parallel: rows [r*N/W, (r+1)*N/W); row-parallel: blocks [r*nb/W, (r+1)*nb/W) of every row
@@ -233,7 +244,27 @@ def run_ours(args, rank, world, local_rank):
                 one_step(c)
             launches_per_step = L.qmm_launch_count() - n0
             graphs.append(g)
+        # one graph per full pass over the weight copies (fewer graph launches:
+        # no launch gap between the steps of a pass)
+        pass_graph = None
+        if copies > 1:
+            pass_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(pass_graph, stream=stream):
+                for c in range(copies):
+                    one_step(c)
     torch.cuda.synchronize(dev)
+
+    def run_steps(n):
+        """Exactly n steps, step i on weight copy i % copies: whole passes
+        where they fit, single-step graphs for the rest."""
+        i = 0
+        while i < n:
+            if pass_graph is not None and i % copies == 0 and i + copies <= n:
+                pass_graph.replay()
+                i += copies
+            else:
+                graphs[i % copies].replay()
+                i += 1
 
     def barrier():
         if world > 1:
@@ -241,8 +272,7 @@ def run_ours(args, rank, world, local_rank):
 
     # warm-up
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            graphs[i % copies].replay()
+        run_steps(args.warmup)
     stream.synchronize()
 
     # timed region: K steps, events on the launching stream, max over ranks
@@ -250,15 +280,13 @@ def run_ours(args, rank, world, local_rank):
     sampler = ClockSampler(local_rank)
     with sampler:
         with torch.cuda.stream(stream):
-            for i in range(max(args.warmup, 3)):  # clock soak right before the timed region
-                graphs[i % copies].replay()
+            run_steps(max(args.warmup, 3))  # clock soak right before the timed region
         barrier()
         torch.cuda.synchronize(dev)
         n_before = len(sampler.samples)
         with torch.cuda.stream(stream):
             e0.record(stream)
-            for i in range(args.steps):
-                graphs[i % copies].replay()
+            run_steps(args.steps)
             e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
@@ -282,9 +310,9 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = load_peaks()
     clocks = sampler.summary()
     clocks["samples_in_timed_region"] = n_timed
-    for g in graphs:
-        del g
+    # graphs that hold NCCL calls are released before the process group goes
     graphs.clear()
+    pass_graph = None
     if rank == 0:
         line = {
             "metric": "quant GEMV HBM GB/s",
@@ -308,7 +336,8 @@ def run_ours(args, rank, world, local_rank):
                 "parallelism": f"tp{world}" if world > 1 else "single",
                 "l2": f"{copies} weight copies rotated" + (" (>L2)" if copies > 1 else "; weights > L2"),
                 "algorithmic_bytes_per_step": steps_bytes,
-                "graph": "one CUDA graph per weight copy; PDL between kernels",
+                "graph": "one CUDA graph per pass over the weight copies (single-step graphs for the rest of K); "
+                         "PDL between kernels",
             },
             "roofline": {
                 "bound": "hbm",
@@ -318,8 +347,10 @@ def run_ours(args, rank, world, local_rank):
                 "frac": round(value / world / peak, 4),
                 "peak_kind": peak_kind,
                 "traffic": profiled_traffic(args.workload),
-                "note": "achieved = per-GPU algorithmic bytes / timed-region duration (includes the x-prep kernels "
-                        "and, for N>1, collectives); GEMV kernel is the dominant kernel",
+                "note": "achieved = per-GPU algorithmic bytes / timed-region duration, timed with CUDA events on the "
+                        "launching stream: the GEMV launches back to back (plus, for large shapes, their activation-"
+                        "prep launches and, for N>1, the collectives); the GEMV kernel is the dominant kernel "
+                        "(launch shares under profiles/)",
             },
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
@@ -537,6 +568,8 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
+    ap.add_argument("--copies", type=int, default=None,
+                    help="weight copies rotated (default: the workload's; fewer for short profiling runs)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

@@ -135,6 +135,7 @@ int check_shape(int dt, size_t m, size_t k, size_t n, size_t w_len) {
 
 size_t workspace_for(int dt, int act, size_t m, size_t n, size_t k, int dev) {
     if (m == 0 || n == 0) return 0;
+    if (gemm_supported(dt, act == QMM_ACT_Q8_0, (int)m, (int)n, (int)k)) return gemm_workspace_bytes((int)m, (int)k);
     const size_t rows = m < kMaxGemvRows ? m : kMaxGemvRows;
     GemvPlan p;
     if (!gemv_plan(dt, act == QMM_ACT_Q8_0, (int)rows, (int)n, (int)k, num_sms(dev), &p)) return 0;
@@ -150,6 +151,13 @@ int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size
     const int dev = current_device();
     if (dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
     int* err = device_error_word(dev);
+    // prefill-sized M: one tensor-core GEMM over all rows
+    if (gemm_supported(dt, act == QMM_ACT_Q8_0, (int)m, (int)n, (int)k)) {
+        if (gemm_workspace_bytes((int)m, (int)k) > ws_bytes) return fail(QMM_ERR_INVALID_INPUT, "workspace too small");
+        cudaError_t e = launch_gemm(dt, w, x, y, (int)m, (int)n, (int)k, ws, err, st, immutable_w);
+        if (e != cudaSuccess) return cuda_fail(e, "launch_gemm");
+        return QMM_OK;
+    }
     for (size_t r0 = 0; r0 < m; r0 += kMaxGemvRows) {
         const size_t rows = (m - r0) < kMaxGemvRows ? (m - r0) : kMaxGemvRows;
         GemvPlan p;

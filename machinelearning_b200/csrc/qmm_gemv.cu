@@ -498,6 +498,21 @@ bool resident_plan(GemvPlan& q, int num_sms) {
 
 }  // namespace
 
+cudaError_t encode_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t dim0,
+                          uint64_t dim1, uint64_t row_stride_bytes, uint32_t box0, uint32_t box1,
+                          CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)dim0, (cuuint64_t)dim1};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_stride_bytes};
+    const cuuint32_t box[2] = {box0, box1};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(out, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t ensure_dynamic_smem(const void* fn, size_t bytes) {
     static std::mutex mu;
     static std::map<std::pair<int, const void*>, size_t> done;

@@ -123,6 +123,21 @@ int resident_capacity(int qt, int loader, int nt, int cluster, size_t smem);
 // (cached per device and kernel).
 cudaError_t ensure_dynamic_smem(const void* fn, size_t bytes);
 
+// A 2-D TMA tensor map (dim0 innermost, in elements; zero fill out of bounds).
+cudaError_t encode_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t dim0,
+                          uint64_t dim1, uint64_t row_stride_bytes, uint32_t box0, uint32_t box1,
+                          CUtensorMapSwizzle swizzle);
+
+// ---- prefill GEMM (qmm_gemm.cu): tcgen05 tensor cores, f32 activations ------------------
+// y[M,N] = x[M,K] . W[N,K]^T for f32-activation calls with M >= kGemmMinRows
+// and a weight row pitch that is a multiple of 16 bytes.
+constexpr int kGemmMinRows = 17;
+bool gemm_supported(int qt, bool native, int M, int N, int K);
+size_t gemm_workspace_bytes(int M, int K);
+// ws: gemm_workspace_bytes(M, K) bytes, 256-byte aligned.
+cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
+                        int* err, cudaStream_t st, bool weights_immutable);
+
 int* device_error_word(int device);
 
 // Launch accounting (qmm_launch_count): every launch site calls note_launch().

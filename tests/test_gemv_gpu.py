@@ -85,13 +85,28 @@ def assert_bits_equal(y, ref, msg=""):
     np.testing.assert_array_equal(y[~ny].view(np.uint32), ref[~nr].view(np.uint32), err_msg=msg)
 
 
+def gemm_path(dt, act, m, k):
+    """True when the library runs this call on the tensor-core GEMM: f32
+    activations, M >= 17 and a weight row pitch that is a multiple of 16 bytes
+    (qmm_kernels.cuh: gemm_supported)."""
+    return act == 0 and m >= 17 and ((k // 32) * BB[dt]) % 16 == 0
+
+
+# The GEMM rounds both operands to f16 (unit roundoff 2^-11): the norm-wise
+# error stays ~3e-4 (the 1e-3 contract holds), but per-element errors are
+# Gaussian-tailed with sigma ~4e-4 of the output rms, so the largest of ~10^6
+# outputs sits near 5 sigma. Its per-element outlier guard is 4e-3; the GEMV
+# paths carry activations as f16 hi+lo (~1e-5) and keep the 1e-3 guard.
+GEMM_ELEM_RTOL = 4e-3
+
+
 def check(oracle, torch, qlib, dt, act, x, w, m, k, n):
     y = gpu_matmul(torch, qlib, dt, act, x, w, m, k, n)
     ref = getattr(oracle, ORACLE_FN[(dt, act)])(x, w, m, k, n)
     if act == 1:
         assert_bits_equal(y, ref, f"native dt={dt} m={m} k={k} n={n} not bit-exact")
         return 0.0
-    return assert_close_rel(y, ref, 1e-3)
+    return assert_close_rel(y, ref, 1e-3, GEMM_ELEM_RTOL if gemm_path(dt, act, m, k) else None)
 
 
 def device_error_clear(qlib):
@@ -130,6 +145,54 @@ def test_config5_llama70b_q4_0(oracle, torch_cuda, qlib, m, shape):
     k, n = shape
     w = random_blocks(Q4_0, n, k, seed=k + n)
     x = np.random.default_rng(7).normal(0, 1, m * k).astype(np.float32)
+    check(oracle, torch_cuda, qlib, Q4_0, 0, x, w, m, k, n)
+
+
+def test_config3_prefill_q4_0_gemm(oracle, torch_cuda, qlib):
+    """M = 512 tokens, K = 4096, N = 11008 Q4_0 through the
+    tensor-core GEMM (f16 operands, f32 accumulation, bound 1e-3). Output rows
+    are independent, so the oracle runs on a spread of 64 token rows."""
+    m, k, n = 512, 4096, 11008
+    w = make_weights(oracle, Q4_0, n, k, seed=3)
+    x = np.random.default_rng(300).normal(0, 1, m * k).astype(np.float32)
+    y = gpu_matmul(torch_cuda, qlib, Q4_0, 0, x, w, m, k, n).reshape(m, n)
+    rows = np.r_[0:16, 120:136, 250:266, 496:512]
+    ref = oracle.matmul_f32_q4(x.reshape(m, k)[rows].ravel(), w, len(rows), k, n).reshape(len(rows), n)
+    rel = assert_close_rel(y[rows].ravel(), ref.ravel(), 1e-3, GEMM_ELEM_RTOL)
+    assert rel < 6e-4, rel  # f16 rounding of both operands: ~3e-4 expected
+
+
+# Tensor-core GEMM shapes: ragged M (token tiles of 128), ragged N (weight
+# tiles of 128), K not a multiple of the 256-element raw chunk or the 64-element
+# K step (zero-filled boxes), all three block types.
+GEMM = [
+    (Q4_0, 17, 256, 64),
+    (Q4_0, 32, 8192, 200),
+    (Q4_0, 129, 512, 1000),
+    (Q8_0, 17, 512, 96),
+    (Q8_0, 64, 2048, 128),
+    (Q8_0, 200, 768, 333),
+    (Q4_1, 40, 384, 130),
+    (Q4_1, 300, 1024, 64),
+]
+
+
+@pytest.mark.parametrize("case", range(len(GEMM)))
+def test_gemm_shapes(oracle, torch_cuda, qlib, case):
+    dt, m, k, n = GEMM[case]
+    w = make_weights(oracle, dt, n, k, seed=700 + case)
+    x = np.random.default_rng(750 + case).normal(0, 1, m * k).astype(np.float32)
+    check(oracle, torch_cuda, qlib, dt, 0, x, w, m, k, n)
+    check(oracle, torch_cuda, qlib, dt, 1, x, w, m, k, n)  # Q8_0 activations: GEMV, bit-exact
+
+
+@pytest.mark.parametrize("scale", [1e-30, 1e4, 1e30])
+def test_gemm_activation_magnitudes(oracle, torch_cuda, qlib, scale):
+    """Per-row power-of-two scaling keeps any finite f32 activation range."""
+    m, k, n = 40, 1024, 256
+    w = make_weights(oracle, Q4_0, n, k, seed=77)
+    x = (np.random.default_rng(78).normal(0, 1, m * k) * scale).astype(np.float32)
+    x[: k] = 0.0  # an all-zero row
     check(oracle, torch_cuda, qlib, Q4_0, 0, x, w, m, k, n)
 
 

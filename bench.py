@@ -1,7 +1,7 @@
 """Benchmark of the quantized-matmul hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemma-q8-sweep|q4-gemv|llama70b|llama70b-gate]
+                    [--workload gemma-q8-sweep|q4-gemv|llama70b|llama70b-gate|prefill]
 
 Workloads (synthetic, seeded, weights ~N(0, 0.02)
 quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
@@ -18,6 +18,10 @@ quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
   llama70b-gate (one projection of configs[4]): Q4_0 8192->28672, batch 1,
       two weight copies (264 MB > L2); the small case for streaming-kernel
       profiles.
+  prefill: Q4_0 [11008 x 4096] x f32 [512 x 4096], one call per
+      step on the tensor-core GEMM, six weight copies rotated (152 MB > L2);
+      metric "prefill GEMM TFLOP/s" = 2*M*N*K / time, roofline bound "tensor"
+      against the measured dense bf16/f16 peak.
 
 Small decode shapes (all of gemma-q8-sweep and q4-gemv) run as one resident
 GEMV launch per call; larger ones as an activation-prep launch plus the
@@ -70,7 +74,25 @@ WORKLOADS = {
     "llama70b-gate": dict(
         config_index=4, projections=[("gate", 8192, 28672, Q4_0, "col")], batches=[1], copies=2,
         model="Llama-3-70B FFN gate, Q4_0"),
+    "prefill": dict(
+        config_index=2, projections=[("ffn", 4096, 11008, Q4_0, "col")], batches=[512], copies=6,
+        model="Llama-7B FFN, Q4_0, 512-token prefill", metric="flops"),
 }
+
+
+def metric_info(wl):
+    """(metric, unit, divisor) of a workload: HBM bytes for the GEMV workloads,
+    2*M*N*K flops for the prefill GEMM."""
+    if wl.get("metric") == "flops":
+        return "prefill GEMM TFLOP/s", "TFLOP/s", 1e12
+    return "quant GEMV HBM GB/s", "GB/s", 1e9
+
+
+def work(wl, m, k, n, dt):
+    """Algorithmic work of one call in the workload's unit."""
+    if wl.get("metric") == "flops":
+        return 2.0 * m * k * n
+    return alg_bytes(m, k, n, dt)
 
 
 def alg_bytes(m, k, n, dt):
@@ -84,13 +106,15 @@ def host_cores():
         return os.cpu_count() or 1
 
 
-def load_peaks():
+def load_peaks(tensor=False):
+    """HBM GB/s, or dense bf16/f16 TFLOP/s (burst: the kernel is timed alone),
+    from MEASURED_PEAKS.json; else the pool's earlier measurement."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return float(p["bf16_tflops"] if tensor else p["hbm_gbs"]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return (1590.0 if tensor else 6650.0), "fallback"
 
 
 def profiled_traffic(workload):
@@ -230,6 +254,8 @@ def run_ours(args, rank, world, local_rank):
 
     launches_per_step = None  # counted by the library while one step is captured
     steps_bytes = sum(alg_bytes(b, k, n, dt) for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems)
+    steps_work = sum(work(wl, b, k, n, dt) for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems)
+    metric, unit, div = metric_info(wl)
 
     # ---- CUDA graphs: one per weight copy -------------------------------------------------
     graphs = []
@@ -297,7 +323,7 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    value = steps_bytes * args.steps / (ms / 1e3) / 1e9
+    value = steps_work * args.steps / (ms / 1e3) / div
 
     # ---- end to end through the C ABI with host buffers ------------------------------------
     e2e = None if args.no_e2e else run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies)
@@ -307,7 +333,7 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, budget_s=args.cpu_seconds)
 
-    peak, peak_kind = load_peaks()
+    peak, peak_kind = load_peaks(tensor=wl.get("metric") == "flops")
     clocks = sampler.summary()
     clocks["samples_in_timed_region"] = n_timed
     # graphs that hold NCCL calls are released before the process group goes
@@ -315,9 +341,9 @@ def run_ours(args, rank, world, local_rank):
     pass_graph = None
     if rank == 0:
         line = {
-            "metric": "quant GEMV HBM GB/s",
+            "metric": metric,
             "value": round(value, 1),
-            "unit": "GB/s",
+            "unit": unit,
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
@@ -325,7 +351,9 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "f32 activations x Q4_0/Q8_0 blocks (f16 tensor-core MMA, f32 accumulate)",
+            "dtype": ("f32 activations rounded to f16 x Q4_0 blocks dequantised to f16 (tcgen05 MMA, f32 accumulate)"
+                      if wl.get("metric") == "flops" else
+                      "f32 activations x Q4_0/Q8_0 blocks (f16 tensor-core MMA, f32 accumulate)"),
             "data": "synthetic: seeded x~N(0,1); weights ~N(0,0.02) quantised on device (bit-exact reference quantiser)",
             "config": {
                 "workload": args.workload,
@@ -336,18 +364,19 @@ def run_ours(args, rank, world, local_rank):
                 "parallelism": f"tp{world}" if world > 1 else "single",
                 "l2": f"{copies} weight copies rotated" + (" (>L2)" if copies > 1 else "; weights > L2"),
                 "algorithmic_bytes_per_step": steps_bytes,
+                "algorithmic_flops_per_step": sum(2 * b * k * n for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems),
                 "graph": "one CUDA graph per pass over the weight copies (single-step graphs for the rest of K); "
                          "PDL between kernels",
             },
             "roofline": {
-                "bound": "hbm",
+                "bound": "tensor" if wl.get("metric") == "flops" else "hbm",
                 "achieved": round(value / world, 1),
                 "peak": peak,
-                "unit": "GB/s",
+                "unit": unit,
                 "frac": round(value / world / peak, 4),
                 "peak_kind": peak_kind,
                 "traffic": profiled_traffic(args.workload),
-                "note": "achieved = per-GPU algorithmic bytes / timed-region duration, timed with CUDA events on the "
+                "note": "achieved = per-GPU algorithmic work (bytes, or 2*M*N*K flops) / timed-region duration, timed with CUDA events on the "
                         "launching stream: the GEMV launches back to back (plus, for large shapes, their activation-"
                         "prep launches and, for N>1, the collectives); the GEMV kernel is the dominant kernel "
                         "(launch shares under profiles/)",
@@ -393,8 +422,9 @@ def run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies):
     for i in range(steps):
         step(i % copies)
     dt_s = time.perf_counter() - t0
-    bytes_step = sum(alg_bytes(b, k, n, d) for b in wl["batches"] for (_, kl, nl, d, kind, k, n) in problems)
-    return {"value": round(bytes_step * steps / dt_s / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+    work_step = sum(work(wl, b, k, n, d) for b in wl["batches"] for (_, kl, nl, d, kind, k, n) in problems)
+    _, unit, div = metric_info(wl)
+    return {"value": round(work_step * steps / dt_s / div, 1), "unit": unit, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(dt_s * 1e3 / steps, 4),
             "path": "qmm_linear_forward_host (C ABI, pinned host x/y, one synchronous call per GEMV)"}
 
@@ -445,8 +475,9 @@ def e2e_tp(args, wl, problems, weights, L, sp, stream, world, dev, copies):
     t = torch.tensor([dt_s], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dt_s = float(t.item())
-    bytes_step = sum(alg_bytes(b, k, n, d) for b in wl["batches"] for (_, kl, nl, d, kind, k, n) in problems)
-    return {"value": round(bytes_step * steps / dt_s / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+    work_step = sum(work(wl, b, k, n, d) for b in wl["batches"] for (_, kl, nl, d, kind, k, n) in problems)
+    _, unit, div = metric_info(wl)
+    return {"value": round(work_step * steps / dt_s / div, 1), "unit": unit, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(dt_s * 1e3 / steps, 4),
             "path": "pinned host x -> qmm_linear_forward on the shard -> NCCL join -> pinned host y, per GEMV"}
 
@@ -485,7 +516,7 @@ def cpu_step(oracle, wl, ws, xs, c):
             w, rows = ws[c][i]
             fn = oracle.matmul_f32_q8 if dt == Q8_0 else oracle.matmul_f32_q4
             fn(xs[(b, i)], w, b, k, rows)
-            bytes_done += alg_bytes(b, k, rows, dt)
+            bytes_done += work(wl, b, k, rows, dt)
     return bytes_done
 
 
@@ -512,7 +543,8 @@ def cpu_baseline(wl, budget_s=10.0):
         done += cpu_step(oracle, wl, ws, xs, steps % len(ws))
         steps += 1
     dt_s = time.perf_counter() - t0
-    return {"value": round(done / dt_s / 1e9, 3), "unit": "GB/s", "cores": oracle.threads(), "kind": "port",
+    _, unit, div = metric_info(wl)
+    return {"value": round(done / dt_s / div, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",
             "sample": f"{steps} steps over {len(ws)} layer copies, {frac:.3f} of each projection's rows, "
                       f"{dt_s:.1f} s; AVX2+FMA restatement of the reference's CPU path, OpenMP over all cores"}
 
@@ -532,12 +564,13 @@ def run_reference(args, rank, world):
     for i in range(args.steps):
         done += cpu_step(oracle, wl, ws, xs, i % len(ws))
     dt_s = time.perf_counter() - t0
-    value = done / dt_s / 1e9
+    metric, unit, div = metric_info(wl)
+    value = done / dt_s / div
     line = {
         "impl": "reference",
-        "metric": "quant GEMV HBM GB/s",
-        "value": round(value, 3),
-        "unit": "GB/s",
+        "metric": metric,
+        "value": round(value, 4),
+        "unit": unit,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
@@ -549,11 +582,11 @@ def run_reference(args, rank, world):
         "data": "synthetic: seeded x~N(0,1), random well-formed blocks",
         "config": {"workload": args.workload, "baseline_config_index": wl["config_index"], "model": wl["model"],
                    "batches": wl["batches"], "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": oracle.threads(), "kind": "port",
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": oracle.threads(), "kind": "port",
                          "sample": f"{frac:.4f} of each projection's rows per step, {len(ws)} layer copies; "
                                    "C++ restatement of matmul_f32_q8/_q4 (AVX2+FMA dispatch, OpenMP); "
                                    "the Rust reference cannot be built here (no cargo)"},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 

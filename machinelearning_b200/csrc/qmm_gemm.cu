@@ -1,4 +1,4 @@
-// Prefill GEMM for sm_100a: tcgen05 tensor cores with a TMEM accumulator.
+// Prefill GEMM for sm_100a: tcgen05 tensor cores with TMEM accumulators.
 //
 // y[M, N] = x[M, K] . W[N, K]^T for f32 activations and GGUF block weights
 // (Q4_0 / Q4_1 / Q8_0 rows, raw bytes), M >= kGemmMinRows. Replaces the M > 4
@@ -9,29 +9,36 @@
 // Two launches per call:
 //   1. gemm_xprep: each activation row is scaled by a power of two (its max
 //      lands in [2^14, 2^15)) and rounded to f16; the scale is kept per row.
-//   2. gemm_kernel: one CTA per 128-token x 128-weight-row output tile, full K,
-//      six warps:
-//        warp 0  TMA producer: x16 tiles [128 tokens x 64] with 128-byte
-//                swizzle (the canonical K-major UMMA layout) and raw weight
-//                chunks [128 rows x 8 blocks] (2-D boxes of the GGUF bytes);
-//        warp 1  allocates 128 TMEM columns; one thread issues
-//                tcgen05.mma.kind::f16 (M 128, N 128, K 16, both operands from
-//                shared memory through descriptors) and commits to mbarriers;
-//        warps 2-5 dequantise one weight row each per K step (magic-number f16
-//                pairs, one f16 rounding of d*q, d*(n-8) or d*n+m) into the
-//                swizzled B tile, then read the accumulator back with
-//                tcgen05.ld and write y = acc * row scale.
-//      Stages: 4 x (A 16 KB + B 16 KB) operand stages, 2 raw chunk stages;
-//      every wait is bounded (error word on timeout, in-flight copies drained).
+//   2. gemm_kernel<QT, T>: one CTA per output tile of T x 128 tokens by 128
+//      weight rows, full K, eleven warps:
+//        warp 0    TMA producer of T x16 tiles [128 tokens x 64] per K step
+//                  with 128-byte swizzle (the canonical K-major UMMA layout);
+//        warp 10   TMA producer of raw weight chunks [128 rows x 8 blocks]
+//                  (2-D boxes of the GGUF bytes);
+//        warp 1    allocates T x 128 TMEM columns; one thread issues
+//                  tcgen05.mma.kind::f16 (M 128, N 128, K 16, both operands
+//                  read from shared memory through descriptors) into T
+//                  accumulators and commits to mbarriers;
+//        warps 2-9 dequantise: each thread one 32-weight block of one row per
+//                  K step (magic-number f16 pairs, one f16 rounding of d*q,
+//                  d*(n-8) or d*n+m), written into the swizzled B tile; then
+//                  they read the accumulators back with tcgen05.ld (two warps
+//                  per TMEM lane quarter) into a staging tile and write
+//                  y = acc * row scale as whole coalesced rows.
+//      One dequantised B tile feeds T accumulators: T = 2 for M > 128 halves
+//      the dequantisation per flop. Rings: x16 tiles 6 (T = 1) or 3-4 (T = 2)
+//      stages, weight tiles 3, raw chunks 2; every wait is bounded (error word
+//      on timeout, in-flight copies drained before exit).
 //
 // Numerics: both operands are rounded to f16 (unit roundoff 2^-11), products
-// are exact and accumulate in f32: relative error ~4e-4 of ||y|| on N(0, 1)
+// are exact and accumulate in f32: relative error ~3e-4 of ||y|| on N(0, 1)
 // activations, inside the 1e-3 contract (the GEMV paths carry activations as
 // f16 hi+lo and stay near 1e-5).
 #include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <cstring>
+#include <type_traits>
 
 #include "qmm_common.cuh"
 #include "qmm_kernels.cuh"
@@ -40,14 +47,22 @@ namespace qmm {
 
 namespace {
 
-constexpr int BM = 128;                 // tokens per tile (MMA M, TMEM lanes)
-constexpr int BN = 128;                 // weight rows per tile (MMA N, TMEM columns)
-constexpr int BK = 64;                  // f16 elements per K step: one 128-byte swizzle row
-constexpr int kStepsPerChunk = 4;       // a raw chunk is 8 blocks = 256 elements
-constexpr int S = 4;                    // operand stages
-constexpr int SR = 2;                   // raw chunk stages
-constexpr int kGemmThreads = 192;
+constexpr int BM = 128;            // tokens per accumulator (MMA M, TMEM lanes)
+constexpr int BN = 128;            // weight rows per tile (MMA N, TMEM columns)
+constexpr int BK = 64;             // f16 elements per K step: one 128-byte swizzle row
+constexpr int kStepsPerChunk = 4;  // a raw chunk is 8 blocks = 256 elements
+constexpr int SR = 2;              // raw chunk stages
+constexpr int kDqWarps = 8;        // dequantising (then epilogue) warps
+constexpr int kDqThreads = 32 * kDqWarps;
+constexpr int kGemmThreads = 64 + kDqThreads + 32;  // + the raw-chunk producer warp
 constexpr uint32_t kTileBytes = BM * BK * 2;  // 16 KB: 128 rows x 128 bytes
+
+// Operand rings: the x16 (A) ring is the deeper one -- its TMA loads take
+// 1.5-2 us to land under load, and a stage is refilled only once the MMAs
+// that read it have completed -- while dequantised weight tiles (B) are ready
+// ~0.3 us after their raw chunk is. Sized to fill 227 KB with the raw ring.
+__host__ __device__ constexpr int a_stages(int qt, int T) { return T == 1 ? 6 : (qt == kQ8_0 ? 3 : 4); }
+__host__ __device__ constexpr int b_stages(int, int) { return 3; }
 
 // Raw chunk row pitch in shared memory (= the TMA box's inner extent): 8
 // blocks, padded so consecutive rows sit an odd number of 16-byte units apart
@@ -65,8 +80,10 @@ struct GArgs {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-size_t gemm_smem_bytes(int qt) {
-    return 1024 + 2 * S * (size_t)kTileBytes + (size_t)SR * BN * raw_pitch(qt) + (3 * S + 2 * SR + 1) * 8 + 16;
+size_t gemm_smem_bytes(int qt, int T) {
+    const int SA = a_stages(qt, T), SB = b_stages(qt, T);
+    return 1024 + (size_t)(SA * T + SB) * kTileBytes + (size_t)SR * BN * raw_pitch(qt) + (2 * SA + 2 * SB + 2 * SR + 1) * 8 +
+           16;
 }
 
 // ---- tcgen05 / TMEM --------------------------------------------------------------
@@ -139,6 +156,10 @@ __device__ __forceinline__ uint32_t h2_u32(__half2 h) {
     memcpy(&v, &h, 4);
     return v;
 }
+__device__ __forceinline__ __half2 half2_from_bits(uint32_t bits16) {
+    const __half h = __ushort_as_half((unsigned short)bits16);
+    return __halves2half2(h, h);
+}
 
 // Q8_0: 4 int8 -> two f16 pairs d*q (elements in order).
 __device__ __forceinline__ void q8_pairs(uint32_t w, __half2 d2, uint32_t& p01, uint32_t& p23) {
@@ -159,49 +180,23 @@ __device__ __forceinline__ uint32_t q4_value(uint32_t h, __half2 d2, __half2 m2)
     return h2_u32(__hfma2(__hsub2(as_h2(h), __float2half2_rn(1024.0f)), d2, m2));
 }
 
-// One Q4 block (payload words p[0..3], GGML order: low nibble of byte j is
-// element j, high nibble element j+16) -> four 16-byte chunks of 8 halves.
-template <int QT>
-__device__ __forceinline__ void q4_block(const uint32_t (&p)[4], __half2 d2, __half2 m2, uint4 (&c)[4]) {
-    uint32_t lo[8], hi[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t t01 = __byte_perm(p[i], 0u, 0x4140), t23 = __byte_perm(p[i], 0u, 0x4342);
-        lo[2 * i] = q4_value<QT>(lo_nibbles(t01), d2, m2);
-        lo[2 * i + 1] = q4_value<QT>(lo_nibbles(t23), d2, m2);
-        hi[2 * i] = q4_value<QT>(hi_nibbles(t01), d2, m2);
-        hi[2 * i + 1] = q4_value<QT>(hi_nibbles(t23), d2, m2);
-    }
-    c[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // elements 0-7
-    c[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);  // 8-15
-    c[2] = make_uint4(hi[0], hi[1], hi[2], hi[3]);  // 16-23
-    c[3] = make_uint4(hi[4], hi[5], hi[6], hi[7]);  // 24-31
-}
-__device__ __forceinline__ void q8_block(const uint32_t (&p)[8], __half2 d2, uint4 (&c)[4]) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        uint32_t a0, a1, b0, b1;
-        q8_pairs(p[2 * i], d2, a0, a1);
-        q8_pairs(p[2 * i + 1], d2, b0, b1);
-        c[i] = make_uint4(a0, a1, b0, b1);
-    }
-}
-__device__ __forceinline__ __half2 half2_from_bits(uint32_t bits16) {
-    const __half h = __ushort_as_half((unsigned short)bits16);
-    return __halves2half2(h, h);
+// Payload word i of a block whose payload starts at byte P of the loaded words.
+template <int P>
+__device__ __forceinline__ uint32_t payload_word(const uint32_t* W, int i) {
+    if constexpr (P % 4 == 0) return W[P / 4 + i];
+    return __byte_perm(W[P / 4 + i], W[P / 4 + i + 1], 0x5432);
 }
 
-// One K step (two blocks) of one weight row: the row's raw chunk in shared
-// memory (16-byte aligned, `pitch` bytes), K step KK of the chunk, written as
-// 8 swizzled 16-byte chunks at `dst` (the row's 128 bytes of the B tile).
-template <int QT, int KK>
-__device__ __forceinline__ void dequant_step(const uint8_t* row, uint8_t* dst, int r7) {
+// One block of one weight row: the block starts OFF bytes into the row's raw
+// chunk (16-byte aligned, in shared memory); its 32 weights become four
+// 16-byte chunks of 8 f16 (elements in order) stored at chunk positions
+// CB..CB+3 of the row's 128 swizzled bytes at `dst`.
+template <int QT, int OFF, int CB>
+__device__ __forceinline__ void dequant_block(const uint8_t* row, uint8_t* dst, int r7) {
     constexpr int BB = block_bytes(QT);
-    constexpr int W0 = (2 * BB * KK) / 4;  // first word of this K step's two blocks
-    constexpr int U0 = W0 / 4;              // first aligned 16-byte unit
-    constexpr int O = W0 - 4 * U0;          // word offset inside it
-    constexpr int NW = (2 * BB) / 4;        // words of two blocks
-    constexpr int NU = (O + NW + 3) / 4;
+    constexpr int U0 = OFF / 16;           // first aligned 16-byte unit
+    constexpr int ST = OFF - 16 * U0;      // block start inside the loaded bytes
+    constexpr int NU = (ST + BB + 15) / 16;
     uint32_t W[4 * NU];
     const uint4* src = reinterpret_cast<const uint4*>(row) + U0;
 #pragma unroll
@@ -212,55 +207,45 @@ __device__ __forceinline__ void dequant_step(const uint8_t* row, uint8_t* dst, i
         W[4 * u + 2] = v.z;
         W[4 * u + 3] = v.w;
     }
-    uint4 ca[4], cb[4];
+    const uint32_t hw = W[ST / 4];
+    const uint32_t dbits = (ST % 4 == 0) ? (hw & 0xffffu) : (hw >> 16);
+    const __half2 d2 = half2_from_bits(dbits);
+    uint4 c[4];
     if constexpr (QT == kQ8_0) {
-        // block A at byte 0 (header low half of W[O], payload shifted by 2 bytes),
-        // block B at byte 34 (header high half of W[O+8], payload W[O+9..O+16])
-        uint32_t pa[8], pb[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            pa[i] = __byte_perm(W[O + i], W[O + i + 1], 0x5432);
-            pb[i] = W[O + 9 + i];
-        }
-        q8_block(pa, half2_from_bits(W[O] & 0xffffu), ca);
-        q8_block(pb, half2_from_bits(W[O + 8] >> 16), cb);
-    } else if constexpr (QT == kQ4_0) {
-        // block A at byte 0, block B at byte 18 (header high half of W[O+4])
-        uint32_t pa[4], pb[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            pa[i] = __byte_perm(W[O + i], W[O + i + 1], 0x5432);
-            pb[i] = W[O + 5 + i];
+            uint32_t a0, a1, b0, b1;
+            q8_pairs(payload_word<ST + 2>(W, 2 * i), d2, a0, a1);
+            q8_pairs(payload_word<ST + 2>(W, 2 * i + 1), d2, b0, b1);
+            c[i] = make_uint4(a0, a1, b0, b1);  // elements 8i..8i+7
         }
-        const __half2 z = __float2half2_rn(0.0f);
-        q4_block<QT>(pa, half2_from_bits(W[O] & 0xffffu), z, ca);
-        q4_block<QT>(pb, half2_from_bits(W[O + 4] >> 16), z, cb);
     } else {
-        // Q4_1: [d][m][16 B] x 2, both word aligned
-        uint32_t pa[4], pb[4];
+        constexpr int NOFF = QT == kQ4_1 ? 4 : 2;
+        const __half2 m2 = QT == kQ4_1 ? half2_from_bits(hw >> 16) : __float2half2_rn(0.0f);
+        uint32_t lo[8], hi[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            pa[i] = W[O + 1 + i];
-            pb[i] = W[O + 6 + i];
+            // GGML order: low nibble of byte j is element j, high nibble element j + 16
+            const uint32_t p = payload_word<ST + NOFF>(W, i);
+            const uint32_t t01 = __byte_perm(p, 0u, 0x4140), t23 = __byte_perm(p, 0u, 0x4342);
+            lo[2 * i] = q4_value<QT>(lo_nibbles(t01), d2, m2);
+            lo[2 * i + 1] = q4_value<QT>(lo_nibbles(t23), d2, m2);
+            hi[2 * i] = q4_value<QT>(hi_nibbles(t01), d2, m2);
+            hi[2 * i + 1] = q4_value<QT>(hi_nibbles(t23), d2, m2);
         }
-        q4_block<QT>(pa, half2_from_bits(W[O] & 0xffffu), half2_from_bits(W[O] >> 16), ca);
-        q4_block<QT>(pb, half2_from_bits(W[O + 5] & 0xffffu), half2_from_bits(W[O + 5] >> 16), cb);
+        c[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // elements 0-7
+        c[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);  // 8-15
+        c[2] = make_uint4(hi[0], hi[1], hi[2], hi[3]);  // 16-23
+        c[3] = make_uint4(hi[4], hi[5], hi[6], hi[7]);  // 24-31
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        *reinterpret_cast<uint4*>(dst + ((c ^ r7) << 4)) = ca[c];
-        *reinterpret_cast<uint4*>(dst + (((c + 4) ^ r7) << 4)) = cb[c];
-    }
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(dst + (((CB + i) ^ r7) << 4)) = c[i];
 }
 
-template <int QT>
-__device__ __forceinline__ void dequant_kstep(const uint8_t* row, uint8_t* dst, int r7, int kk) {
-    switch (kk) {
-        case 0: dequant_step<QT, 0>(row, dst, r7); break;
-        case 1: dequant_step<QT, 1>(row, dst, r7); break;
-        case 2: dequant_step<QT, 2>(row, dst, r7); break;
-        default: dequant_step<QT, 3>(row, dst, r7); break;
-    }
+// Block BLK (0 or 1) of K step KK of a raw chunk.
+template <int QT, int KK, int BLK>
+__device__ __forceinline__ void dequant_kstep(const uint8_t* row, uint8_t* dst, int r7) {
+    dequant_block<QT, block_bytes(QT) * (2 * KK + BLK), 4 * BLK>(row, dst, r7);
 }
 
 // ---- activation prep: x f32 -> x16 f16 with a power-of-two scale per row ---------------
@@ -297,35 +282,46 @@ __global__ void gemm_xprep_kernel(const float* __restrict__ x, int M, int K, __h
     if (threadIdx.x == 0) xs[m] = __int_as_float((e + 127) << 23);
 }
 
-template <int QT>
+template <int QT, int T>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GArgs a) {
+    constexpr int SA = a_stages(QT, T), SB = b_stages(QT, T);
+    constexpr int PITCH = raw_pitch(QT);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int PITCH = raw_pitch(QT);
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + S * kTileBytes;
-    uint8_t* sR = smem + 2 * S * kTileBytes;
+    uint8_t* sA = smem;                        // [SA][T] x16 tiles
+    uint8_t* sB = smem + SA * T * kTileBytes;  // [SB] weight tiles
+    uint8_t* sR = sB + SB * kTileBytes;        // [SR] raw chunks
     uint64_t* full_a = reinterpret_cast<uint64_t*>(sR + SR * BN * PITCH);
-    uint64_t* full_b = full_a + S;
-    uint64_t* empty = full_b + S;
-    uint64_t* rfull = empty + S;
+    uint64_t* empty_a = full_a + SA;
+    uint64_t* full_b = empty_a + SA;
+    uint64_t* empty_b = full_b + SB;
+    uint64_t* rfull = empty_b + SB;
     uint64_t* rempty = rfull + SR;
     uint64_t* acc_full = rempty + SR;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * (T * BM);
     const int nchunks = (a.ksteps + kStepsPerChunk - 1) / kStepsPerChunk;
+    // Every CTA starts its K loop at a different raw chunk: CTAs that share a
+    // token tile then fetch different x16 tiles at any moment instead of all
+    // hitting the same L2 lines (the sum order differs per tile, results stay
+    // deterministic).
+    const int rot = (int)(blockIdx.x % (unsigned)nchunks);
+    auto chunk_of = [&](int ci) { return ci + rot < nchunks ? ci + rot : ci + rot - nchunks; };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < SA; ++s) {
             mbar_init(&full_a[s], 1);
-            mbar_init(&full_b[s], 128);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty_a[s], 1);
+        }
+        for (int s = 0; s < SB; ++s) {
+            mbar_init(&full_b[s], kDqThreads);
+            mbar_init(&empty_b[s], 1);
         }
         for (int r = 0; r < SR; ++r) {
             mbar_init(&rfull[r], 1);
-            mbar_init(&rempty[r], 128);
+            mbar_init(&rempty[r], kDqThreads);
         }
         mbar_init(acc_full, 1);
         fence_mbar_init();
@@ -333,7 +329,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         prefetch_tmap(&a.tmap_w);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, BN);
+        tmem_alloc(tmem_slot, T * BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -343,44 +339,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     pdl_launch_dependents();
 
     if (warp == 0) {
-        // ------------------------------- TMA producer ---------------------------------
+        // --------------------------- x16 (A) TMA producer ------------------------------
         if (lane == 0) {
             bool ok = true;
-            int r_issued = 0, a_issued = 0;
-            auto issue_raw = [&](int rc) {
-                const int sr = rc % SR;
+            int a_issued = 0;
+            pdl_wait();  // x16 is written by the activation-prep launch
+            for (int ci = 0; ci < nchunks && ok; ++ci) {
+                const int rc = chunk_of(ci);
+                const int nk = min(kStepsPerChunk, a.ksteps - rc * kStepsPerChunk);
+                for (int kk = 0; kk < nk && ok; ++kk) {
+                    const int i = a_issued, s = i % SA;
+                    if (i >= SA && !mbar_wait_bounded(&empty_a[s], ((i / SA) - 1) & 1, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full_a[s], T * kTileBytes);
+#pragma unroll
+                    for (int t = 0; t < T; ++t)
+                        tma_load_2d(sA + (s * T + t) * kTileBytes, &a.tmap_x, (rc * kStepsPerChunk + kk) * BK,
+                                    m0 + t * BM, &full_a[s]);
+                    ++a_issued;
+                }
+            }
+            // every copy this thread started has landed before the CTA can exit
+            for (int i = (a_issued > SA ? a_issued - SA : 0); i < a_issued; ++i)
+                mbar_wait_bounded(&full_a[i % SA], (i / SA) & 1, nullptr);
+        }
+    } else if (warp == kGemmThreads / 32 - 1) {
+        // ------------------------- raw weight chunk producer ----------------------------
+        // A thread of its own, so that waiting for a raw slot never holds up
+        // the x16 stream.
+        if (lane == 0) {
+            int r_issued = 0;
+            auto issue_raw = [&](int ci) {  // the ci-th chunk of this CTA's sequence
+                const int sr = ci % SR;
                 mbar_arrive_expect_tx(&rfull[sr], (uint32_t)(BN * PITCH));
-                tma_load_2d(sR + sr * BN * PITCH, &a.tmap_w, rc * 8 * block_bytes(QT) / 4, n0, &rfull[sr]);
+                tma_load_2d(sR + sr * BN * PITCH, &a.tmap_w, chunk_of(ci) * 8 * block_bytes(QT) / 4, n0, &rfull[sr]);
             };
             // immutable weights: the first chunks may load before the dependency wait
             if (a.weights_immutable)
                 for (; r_issued < SR && r_issued < nchunks; ++r_issued) issue_raw(r_issued);
             pdl_wait();
-            for (int ks = 0; ks < a.ksteps && ok; ++ks) {
-                if (ks % kStepsPerChunk == 0) {
-                    // keep the raw ring SR chunks ahead of the dequantisers
-                    const int want = min(nchunks, ks / kStepsPerChunk + SR);
-                    for (; r_issued < want && ok; ++r_issued) {
-                        if (r_issued >= SR &&
-                            !mbar_wait_bounded(&rempty[r_issued % SR], ((r_issued / SR) - 1) & 1, a.err))
-                            ok = false;
-                        else
-                            issue_raw(r_issued);
-                    }
-                    if (!ok) break;
-                }
-                const int s = ks % S;
-                if (ks >= S && !mbar_wait_bounded(&empty[s], ((ks / S) - 1) & 1, a.err)) {
-                    ok = false;
+            for (; r_issued < nchunks; ++r_issued) {
+                if (r_issued >= SR && !mbar_wait_bounded(&rempty[r_issued % SR], ((r_issued / SR) - 1) & 1, a.err))
                     break;
-                }
-                mbar_arrive_expect_tx(&full_a[s], kTileBytes);
-                tma_load_2d(sA + s * kTileBytes, &a.tmap_x, ks * BK, m0, &full_a[s]);
-                ++a_issued;
+                issue_raw(r_issued);
             }
-            // every copy this thread started has landed before the CTA can exit
-            for (int i = (a_issued > S ? a_issued - S : 0); i < a_issued; ++i)
-                mbar_wait_bounded(&full_a[i % S], (i / S) & 1, nullptr);
             for (int i = (r_issued > SR ? r_issued - SR : 0); i < r_issued; ++i)
                 mbar_wait_bounded(&rfull[i % SR], (i / SR) & 1, nullptr);
         }
@@ -388,74 +392,118 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         // ------------------------------- MMA issuer -----------------------------------
         if (lane == 0) {
             pdl_wait();
-            for (int ks = 0; ks < a.ksteps; ++ks) {
-                const int s = ks % S;
-                if (!mbar_wait_bounded(&full_a[s], (ks / S) & 1, a.err) ||
-                    !mbar_wait_bounded(&full_b[s], (ks / S) & 1, a.err))
+            for (int i = 0; i < a.ksteps; ++i) {  // operand steps in this CTA's chunk order
+                const int sa = i % SA, sb = i % SB;
+                if (!mbar_wait_bounded(&full_a[sa], (i / SA) & 1, a.err) ||
+                    !mbar_wait_bounded(&full_b[sb], (i / SB) & 1, a.err))
                     break;
                 tc_fence_after();
-                const uint64_t ad = sw128_desc(smem_u32(sA + s * kTileBytes));
-                const uint64_t bd = sw128_desc(smem_u32(sB + s * kTileBytes));
+                const uint64_t bd = sw128_desc(smem_u32(sB + sb * kTileBytes));
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k)  // 32-byte steps inside the swizzle atom
-                    mma_f16_ss(tmem, ad + 2 * k, bd + 2 * k, kIdesc, (ks | k) != 0 ? 1u : 0u);
-                mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                for (int t = 0; t < T; ++t) {
+                    const uint64_t ad = sw128_desc(smem_u32(sA + (sa * T + t) * kTileBytes));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)  // 32-byte steps inside the swizzle atom
+                        mma_f16_ss(tmem + t * BN, ad + 2 * k, bd + 2 * k, kIdesc, (i | k) != 0 ? 1u : 0u);
+                }
+                // both stages are free once these MMAs have read them
+                mma_commit(&empty_a[sa]);
+                mma_commit(&empty_b[sb]);
             }
             mma_commit(acc_full);  // arrives when every MMA above has completed
         }
         __syncwarp();
     } else {
-        // --------------------- dequantisers, then the epilogue ---------------------------
-        const int t = threadIdx.x - 64;  // weight row inside the tile
+        // --------------------- dequantisers, then the epilogue (warps 2-9) ----------------
+        const int d = threadIdx.x - 64;
+        const int row = d & (BN - 1);  // weight row inside the tile
+        const int blk = d >> 7;        // which block of the K step (warp-uniform)
+        const int r7 = row & 7;
         pdl_wait();
         bool ok = true;
-        for (int ks = 0; ks < a.ksteps && ok; ++ks) {
-            const int rc = ks / kStepsPerChunk, sr = rc % SR, kk = ks % kStepsPerChunk;
-            if (kk == 0 && !mbar_wait_bounded(&rfull[sr], (rc / SR) & 1, a.err)) {
-                ok = false;
-                break;
-            }
-            const int s = ks % S;
-            if (ks >= S && !mbar_wait_bounded(&empty[s], ((ks / S) - 1) & 1, a.err)) {
-                ok = false;
-                break;
-            }
-            dequant_kstep<QT>(sR + sr * BN * PITCH + t * PITCH, sB + s * kTileBytes + (t >> 3) * 1024 + (t & 7) * 128,
-                              t & 7, kk);
+        auto step = [&](int i, int sr, auto kk) {  // operand step i, K step KK of raw stage sr
+            constexpr int KK = decltype(kk)::value;
+            const int s = i % SB;
+            if (i >= SB && !mbar_wait_bounded(&empty_b[s], ((i / SB) - 1) & 1, a.err)) return false;
+            const uint8_t* rrow = sR + sr * BN * PITCH + row * PITCH;
+            uint8_t* dst = sB + s * kTileBytes + (row >> 3) * 1024 + r7 * 128;
+            if (blk == 0)
+                dequant_kstep<QT, KK, 0>(rrow, dst, r7);
+            else
+                dequant_kstep<QT, KK, 1>(rrow, dst, r7);
             fence_proxy_async_smem();  // generic writes -> visible to the tensor core
             mbar_arrive(&full_b[s]);
-            if (kk == kStepsPerChunk - 1 || ks == a.ksteps - 1) mbar_arrive(&rempty[sr]);
+            return true;
+        };
+        int i = 0;  // operand steps done
+        for (int ci = 0; ci < nchunks && ok; ++ci) {
+            const int sr = ci % SR;
+            if (!mbar_wait_bounded(&rfull[sr], (ci / SR) & 1, a.err)) break;
+            const int nk = min(kStepsPerChunk, a.ksteps - chunk_of(ci) * kStepsPerChunk);
+            ok = step(i, sr, std::integral_constant<int, 0>{});
+            if (ok && nk > 1) ok = step(i + 1, sr, std::integral_constant<int, 1>{});
+            if (ok && nk > 2) ok = step(i + 2, sr, std::integral_constant<int, 2>{});
+            if (ok && nk > 3) ok = step(i + 3, sr, std::integral_constant<int, 3>{});
+            i += nk;
+            mbar_arrive(&rempty[sr]);  // the chunk is consumed
         }
+        // Epilogue: accumulators -> a padded staging tile in the (now idle)
+        // operand rings -> whole output rows, 512 coalesced bytes per warp store.
         const bool acc_ok = mbar_wait_bounded(acc_full, 0, a.err);
         tc_fence_after();
-        const int q = warp & 3;  // this warp's TMEM lane quarter
-        const int m = m0 + q * 32 + lane;
-        const float sc = (m < a.M) ? a.xs[m] : 0.0f;
-#pragma unroll 1
-        for (int cb = 0; cb < BN / 32; ++cb) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32), r);
-            if (acc_ok && m < a.M) {
-                float* yr = a.y + (int64_t)m * a.N + n0 + cb * 32;
-                const int lim = a.N - (n0 + cb * 32);
+        const int q = warp & 3;            // this warp's TMEM lane quarter
+        const int half = (warp - 2) >> 2;  // two warps per quarter split the columns
+        constexpr int YP = BN + 4;         // staging pitch in floats: 16-byte stores conflict free
+        float* ys = reinterpret_cast<float*>(sA);
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (j < lim) yr[j] = __uint_as_float(r[j]) * sc;
+        for (int t = 0; t < T; ++t) {
+            const int r = t * BM + q * 32 + lane;  // token row inside the tile
+#pragma unroll 1
+            for (int cb = half; cb < BN / 32; cb += 2) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * BN + cb * 32), v);
+                float4* dstp = reinterpret_cast<float4*>(ys + r * YP + cb * 32);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    dstp[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                          __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
             }
         }
         tc_fence_before();
+        asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");  // the staging tile is complete
+        const bool vec = ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) && (a.N % 4 == 0);
+        const int n = n0 + 4 * lane;
+        for (int r = warp - 2; r < T * BM && acc_ok; r += kDqWarps) {
+            const int m = m0 + r;
+            if (m >= a.M) break;  // rows are in increasing order
+            const float sc = a.xs[m];
+            const float4 v = *reinterpret_cast<const float4*>(ys + r * YP + 4 * lane);
+            float* yr = a.y + (int64_t)m * a.N + n;
+            if (vec && n + 3 < a.N) {
+                *reinterpret_cast<float4*>(yr) = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
+            } else {
+                if (n < a.N) yr[0] = v.x * sc;
+                if (n + 1 < a.N) yr[1] = v.y * sc;
+                if (n + 2 < a.N) yr[2] = v.z * sc;
+                if (n + 3 < a.N) yr[3] = v.w * sc;
+            }
+        }
     }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, T * BN);
     }
 }
 
-const void* gemm_kernel_for(int qt) {
-    if (qt == kQ8_0) return (const void*)gemm_kernel<kQ8_0>;
-    if (qt == kQ4_0) return (const void*)gemm_kernel<kQ4_0>;
-    return (const void*)gemm_kernel<kQ4_1>;
+template <int QT>
+const void* pick_t(int T) {
+    return T == 1 ? (const void*)gemm_kernel<QT, 1> : (const void*)gemm_kernel<QT, 2>;
+}
+const void* gemm_kernel_for(int qt, int T) {
+    if (qt == kQ8_0) return pick_t<kQ8_0>(T);
+    if (qt == kQ4_0) return pick_t<kQ4_0>(T);
+    return pick_t<kQ4_1>(T);
 }
 
 cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
@@ -510,12 +558,15 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     a.ksteps = (K + BK - 1) / BK;
     a.weights_immutable = weights_immutable ? 1 : 0;
     a.err = err;
-    const void* fn = gemm_kernel_for(qt);
-    const size_t smem = gemm_smem_bytes(qt);
+    // two token tiles per CTA once M needs more than one: each dequantised
+    // weight tile then feeds twice the tensor work
+    const int T = M > BM ? 2 : 1;
+    const void* fn = gemm_kernel_for(qt, T);
+    const size_t smem = gemm_smem_bytes(qt, T);
     e = ensure_dynamic_smem(fn, smem);
     if (e != cudaSuccess) return e;
     void* args[] = {(void*)&a};
-    return launch_ex(fn, dim3((N + BN - 1) / BN, (M + BM - 1) / BM), dim3(kGemmThreads), smem, st, args);
+    return launch_ex(fn, dim3((N + BN - 1) / BN, (M + T * BM - 1) / (T * BM)), dim3(kGemmThreads), smem, st, args);
 }
 
 }  // namespace qmm

@@ -137,6 +137,49 @@ QMM_API int qmm_weight_destroy(qmm_weight* w);
 QMM_API int qmm_weight_info(const qmm_weight* w, int* dtype, size_t* n, size_t* k, const uint8_t** dev_bytes,
                             int* device);
 
+/* Activation functions (qmm_gated_forward: GELU and SiLU; qmm_gated_act_dev:
+ * all three). */
+#define QMM_GELU 0
+#define QMM_SILU 1
+#define QMM_RELU 2
+
+/* Fused projections (reference: Attention::fuse_qkv_weights,
+ * llmserve/llmmodel/layers/main/src/core/attention.rs:306-339, and
+ * FeedForward::fuse_gate_up_weights, feed_forward.rs:147-187).
+ *
+ * qmm_weight_fuse_rows: a new weight whose bytes are the parts' bytes
+ * concatenated in order (rows = sum of the parts' rows), as the reference's
+ * fused QKV / gate+up tensors are; y of the fused weight is the parts' outputs
+ * side by side. Parts: same block type (Q8_0, Q4_0 or Q4_1; the reference fuses
+ * Q8_0 only), same in_features, same device. The parts stay valid.
+ *
+ * qmm_weight_fuse_gate_up: a gate/up weight for qmm_gated_forward. Same rules,
+ * plus gate and up of equal shape [hidden, k]. Its rows interleave gate and up
+ * in groups of 16 (rows 32j..32j+15 = gate rows 16j.., rows 32j+16..32j+31 = up
+ * rows 16j..), zero rows padding hidden to a multiple of 16, so one output tile
+ * of the matmul holds matching gate and up values. qmm_linear_forward rejects
+ * it; qmm_weight_gate_hidden reports hidden (0 for an ordinary weight).
+ *
+ * qmm_gated_forward: out_dev[m][hidden] = act(x . gate^T) * (x . up^T), act =
+ * QMM_GELU or QMM_SILU, the activation applied in the matmul's epilogue (one
+ * launch for decode shapes). The matmul is the f32-activation form for every
+ * block type, as the reference's fused Linear (use_native_* false). */
+QMM_API int qmm_weight_fuse_rows(const qmm_weight* const* parts, size_t count, qmm_weight** out);
+QMM_API int qmm_weight_fuse_gate_up(const qmm_weight* gate, const qmm_weight* up, qmm_weight** out);
+QMM_API int qmm_weight_gate_hidden(const qmm_weight* w, size_t* hidden);
+QMM_API int qmm_gated_forward(const qmm_weight* w, const float* x_dev, size_t m, float* out_dev, int act_fn,
+                              void* stream);
+
+/* 64-bit position-weighted checksum of device bytes: the sum over their
+ * little-endian 32-bit words w_i (the tail zero-padded) of w_i * (2i + 1),
+ * modulo 2^64 -- for verifying that an upload (a GGUF tensor's file range,
+ * reference gguf/main/src/core/parser.rs:501-576) arrived byte for byte.
+ * Synchronous. qmm_checksum_dev: data_dev 4-byte aligned, on the current
+ * device. No counterpart in the reference (its mmap path has no device copy
+ * to verify). */
+QMM_API int qmm_checksum_dev(const void* data_dev, size_t len, void* stream, unsigned long long* out);
+QMM_API int qmm_weight_checksum(const qmm_weight* w, unsigned long long* out);
+
 /* y_dev[m, n] = x_dev[m, k] . W^T on the weight's device, workspace managed by
  * the library (one buffer per device and stream, grown on demand with
  * cudaMalloc; grow it with qmm_reserve_workspace before capturing a graph). */
@@ -180,6 +223,18 @@ QMM_API int qmm_quantize_dev(int dtype, int variant, const float* x_dev, size_t 
 /* Device dequantiser with Tensor::to_f32 semantics. */
 QMM_API int qmm_dequantize_dev(int dtype, const uint8_t* w_dev, size_t w_len, size_t n_elements, float* out_dev,
                                void* stream);
+
+/* Element-wise activation step of FeedForward::forward (reference
+ * layers/main/src/core/feed_forward.rs:198-251), for gate and up produced by
+ * separate matmuls or by one matmul over qmm_weight_fuse_rows(gate, up):
+ * out_dev[m][hidden] = act(gate_dev[i * ld + j]) * up_dev[i * ld + j], in f32,
+ * act = QMM_GELU (tanh approximation), QMM_SILU or QMM_RELU; up_dev may be null
+ * (the ungated activations: out = act(gate)). ld >= hidden is the row stride of
+ * gate and up in elements (2 * hidden for the [gate | up] output of a fused
+ * weight, with up_dev = gate_dev + hidden). Launched with programmatic
+ * dependent launch, so it overlaps the tail of the matmul before it. */
+QMM_API int qmm_gated_act_dev(int act_fn, const float* gate_dev, const float* up_dev, size_t m, size_t hidden,
+                              size_t ld, float* out_dev, void* stream);
 
 #ifdef __cplusplus
 }

@@ -33,6 +33,11 @@ BLOCK_BYTES = {Q4_0: 18, Q4_1: 20, Q8_0: 34}
 ACT_F32 = 0
 ACT_Q8_0 = 1
 
+# activation functions (qmm_gated_forward, qmm_gated_act_dev)
+GELU = 0
+SILU = 1
+RELU = 2
+
 # Every symbol include/qmm.h declares, with (restype, argtypes).
 _P = ctypes.c_void_p
 _SZ = ctypes.c_size_t
@@ -45,6 +50,8 @@ SIGNATURES = {
     "qmm_device_count": (_I, []),
     "qmm_device_error": (_I, [_I, _P]),
     "qmm_launch_count": (ctypes.c_ulonglong, []),
+    "qmm_checksum_dev": (_I, [_P, _SZ, _P, _P]),
+    "qmm_weight_checksum": (_I, [_P, _P]),
     "qmm_matmul_f32_q8": _HOST_MM,
     "qmm_matmul_f32_q8_v2": _HOST_MM,
     "qmm_matmul_f32_q4": _HOST_MM,
@@ -70,6 +77,11 @@ SIGNATURES = {
     "qmm_matmul_dev_noalloc": (_I, [_I, _I, _P, _P, _SZ, _SZ, _SZ, _SZ, _P, _P]),
     "qmm_quantize_dev": (_I, [_I, _I, _P, _SZ, _P, _P, _P]),
     "qmm_dequantize_dev": (_I, [_I, _P, _SZ, _SZ, _P, _P]),
+    "qmm_gated_act_dev": (_I, [_I, _P, _P, _SZ, _SZ, _SZ, _P, _P]),
+    "qmm_weight_fuse_rows": (_I, [_P, _SZ, _P]),
+    "qmm_weight_fuse_gate_up": (_I, [_P, _P, _P]),
+    "qmm_weight_gate_hidden": (_I, [_P, _P]),
+    "qmm_gated_forward": (_I, [_P, _P, _SZ, _P, _I, _P]),
 }
 
 

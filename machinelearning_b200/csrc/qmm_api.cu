@@ -29,6 +29,9 @@ using namespace qmm;
 // Device-side error word (one per device context). Kernels receive its address.
 __device__ int g_qmm_device_error = 0;
 
+// Accumulator of qmm_checksum_dev (one per device context).
+__device__ unsigned long long g_qmm_checksum_acc = 0;
+
 // Scratch for qmm_matmul_dev_noalloc: a fixed, file-scope device array, so that
 // entry point never allocates. Every device that loads the library holds these
 // 4 MiB until the process exits. Host code must not use the symbol itself as a
@@ -145,8 +148,10 @@ size_t workspace_for(int dt, int act, size_t m, size_t n, size_t k, int dev) {
 // The device matmul: GEMV in chunks of <= 64 activation rows.
 // immutable_w: the weights are library-owned (a qmm_weight, complete before
 // any call), so the GEMV may fetch them before waiting on preceding kernels.
+// g: optional gate/up epilogue (y then unused; g.out advances with the rows).
 int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size_t k, size_t n, float* y,
-               void* ws, size_t ws_bytes, cudaStream_t st, bool immutable_w = false) {
+               void* ws, size_t ws_bytes, cudaStream_t st, bool immutable_w = false,
+               const GatedOut& g = GatedOut()) {
     if (m == 0 || n == 0) return QMM_OK;
     const int dev = current_device();
     if (dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
@@ -154,7 +159,7 @@ int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size
     // prefill-sized M: one tensor-core GEMM over all rows
     if (gemm_supported(dt, act == QMM_ACT_Q8_0, (int)m, (int)n, (int)k)) {
         if (gemm_workspace_bytes((int)m, (int)k) > ws_bytes) return fail(QMM_ERR_INVALID_INPUT, "workspace too small");
-        cudaError_t e = launch_gemm(dt, w, x, y, (int)m, (int)n, (int)k, ws, err, st, immutable_w);
+        cudaError_t e = launch_gemm(dt, w, x, y, (int)m, (int)n, (int)k, ws, err, st, immutable_w, g);
         if (e != cudaSuccess) return cuda_fail(e, "launch_gemm");
         return QMM_OK;
     }
@@ -167,7 +172,9 @@ int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size
         p.weights_immutable = immutable_w;
         GemvWorkspace w_s;
         gemv_workspace_carve(p, ws, &w_s);
-        cudaError_t e = launch_gemv(p, w, x + r0 * k, y + r0 * n, w_s, err, st);
+        GatedOut gr = g;
+        if (gr.act >= 0) gr.out += (int64_t)r0 * gr.hidden;
+        cudaError_t e = launch_gemv(p, w, x + r0 * k, y ? y + r0 * n : nullptr, w_s, err, st, false, gr);
         if (e != cudaSuccess) return cuda_fail(e, "launch_gemv");
     }
     return QMM_OK;
@@ -198,6 +205,7 @@ struct qmm_weight {
     int device;
     uint8_t* dev;
     size_t len;
+    size_t gate_hidden;  // > 0: a gate/up weight (rows interleaved in kGateGroup groups)
 };
 
 namespace {
@@ -229,8 +237,27 @@ int weight_create_impl(int dtype, size_t n, size_t k, const uint8_t* src, size_t
         cudaFree(d);
         return cuda_fail(e, "weight upload");
     }
-    qmm_weight* w = new qmm_weight{dtype, n, k, device, d, bytes};
+    qmm_weight* w = new qmm_weight{dtype, n, k, device, d, bytes, 0};
     *out = w;
+    return QMM_OK;
+}
+
+// A new device weight of `rows` rows whose bytes are written by `fill`
+// (device-to-device copies on the legacy stream), synchronised before return.
+template <class F>
+int weight_build(int dtype, size_t rows, size_t k, int device, size_t gate_hidden, F&& fill, qmm_weight** out) {
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    const size_t bytes = rows * row_bytes_of(dtype, k);
+    uint8_t* d = nullptr;
+    QMM_CUDA(cudaMalloc(&d, (bytes + 15) & ~size_t(15)));
+    cudaError_t e = fill(d);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return cuda_fail(e, "weight fuse");
+    }
+    *out = new qmm_weight{dtype, rows, k, device, d, bytes, gate_hidden};
     return QMM_OK;
 }
 
@@ -442,6 +469,90 @@ QMM_API int qmm_weight_create_from_device(int dtype, size_t n, size_t k, const u
     return weight_create_impl(dtype, n, k, dev_bytes, len, device, true, out);
 }
 
+QMM_API int qmm_weight_fuse_rows(const qmm_weight* const* parts, size_t count, qmm_weight** out) {
+    if (!out || !parts || count == 0) return fail(QMM_ERR_INVALID_INPUT, "null pointer or no parts");
+    *out = nullptr;
+    size_t rows = 0;
+    for (size_t i = 0; i < count; ++i) {
+        const qmm_weight* p = parts[i];
+        if (!p) return fail(QMM_ERR_INVALID_INPUT, "null part");
+        if (p->gate_hidden) return fail(QMM_ERR_INVALID_INPUT, "part is a gate/up weight");
+        if (p->dtype != parts[0]->dtype) return fail(QMM_ERR_DTYPE_MISMATCH, "parts differ in block type");
+        if (p->k != parts[0]->k) return fail(QMM_ERR_SHAPE_MISMATCH, "parts differ in in_features");
+        if (p->device != parts[0]->device) return fail(QMM_ERR_INVALID_INPUT, "parts on different devices");
+        rows += p->n;
+    }
+    if (rows > (size_t)INT32_MAX) return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    const int dt = parts[0]->dtype;
+    const size_t k = parts[0]->k;
+    return weight_build(dt, rows, k, parts[0]->device, 0, [&](uint8_t* d) {
+        size_t off = 0;
+        for (size_t i = 0; i < count; ++i) {
+            const size_t b = parts[i]->n * row_bytes_of(dt, k);
+            cudaError_t e = cudaMemcpyAsync(d + off, parts[i]->dev, b, cudaMemcpyDeviceToDevice, 0);
+            if (e != cudaSuccess) return e;
+            off += b;
+        }
+        return cudaSuccess;
+    }, out);
+}
+
+QMM_API int qmm_weight_fuse_gate_up(const qmm_weight* gate, const qmm_weight* up, qmm_weight** out) {
+    if (!out || !gate || !up) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    *out = nullptr;
+    if (gate->gate_hidden || up->gate_hidden) return fail(QMM_ERR_INVALID_INPUT, "part is a gate/up weight");
+    if (gate->dtype != up->dtype) return fail(QMM_ERR_DTYPE_MISMATCH, "gate and up differ in block type");
+    if (gate->k != up->k || gate->n != up->n) return fail(QMM_ERR_SHAPE_MISMATCH, "gate and up differ in shape");
+    if (gate->device != up->device) return fail(QMM_ERR_INVALID_INPUT, "gate and up on different devices");
+    const size_t hidden = gate->n, G = kGateGroup;
+    if (hidden == 0) return fail(QMM_ERR_SHAPE_MISMATCH, "empty gate");
+    const size_t groups = (hidden + G - 1) / G;
+    if (2 * G * groups > (size_t)INT32_MAX) return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    const size_t rb = row_bytes_of(gate->dtype, gate->k);
+    return weight_build(gate->dtype, 2 * G * groups, gate->k, gate->device, hidden, [&](uint8_t* d) {
+        // rows padded to whole groups with zero blocks (d = 0: every product 0)
+        cudaError_t e = cudaMemsetAsync(d, 0, 2 * G * groups * rb, 0);
+        const size_t full = hidden / G, tail = hidden % G;
+        const qmm_weight* src[2] = {gate, up};
+        for (int h = 0; h < 2 && e == cudaSuccess; ++h) {
+            if (full)  // group j of this half -> fused rows [2Gj + hG, 2Gj + hG + G)
+                e = cudaMemcpy2DAsync(d + h * G * rb, 2 * G * rb, src[h]->dev, G * rb, G * rb, full,
+                                      cudaMemcpyDeviceToDevice, 0);
+            if (e == cudaSuccess && tail)
+                e = cudaMemcpyAsync(d + (2 * G * full + h * G) * rb, src[h]->dev + full * G * rb, tail * rb,
+                                    cudaMemcpyDeviceToDevice, 0);
+        }
+        return e;
+    }, out);
+}
+
+QMM_API int qmm_weight_gate_hidden(const qmm_weight* w, size_t* hidden) {
+    if (!w || !hidden) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    *hidden = w->gate_hidden;
+    return QMM_OK;
+}
+
+QMM_API int qmm_gated_forward(const qmm_weight* w, const float* x_dev, size_t m, float* out_dev, int act_fn,
+                              void* stream) {
+    if (!w || !x_dev || !out_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (!w->gate_hidden) return fail(QMM_ERR_INVALID_INPUT, "not a gate/up weight");
+    if (act_fn != QMM_GELU && act_fn != QMM_SILU) return fail(QMM_ERR_INVALID_INPUT, "unknown activation");
+    if (m == 0) return QMM_OK;
+    if (m > (size_t)INT32_MAX) return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    DeviceGuard guard(w->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    const size_t need = workspace_for(w->dtype, QMM_ACT_F32, m, w->n, w->k, w->device);
+    void* ws = nullptr;
+    int rc = get_workspace(w->device, stream, need, &ws);
+    if (rc) return rc;
+    GatedOut g;
+    g.act = act_fn;
+    g.out = out_dev;
+    g.hidden = (int64_t)w->gate_hidden;
+    return run_matmul(w->dtype, QMM_ACT_F32, x_dev, w->dev, m, w->k, w->n, nullptr, ws, need, (cudaStream_t)stream,
+                      /*immutable_w=*/true, g);
+}
+
 QMM_API int qmm_weight_destroy(qmm_weight* w) {
     if (!w) return QMM_OK;
     {
@@ -461,6 +572,32 @@ QMM_API int qmm_weight_info(const qmm_weight* w, int* dtype, size_t* n, size_t* 
     if (dev_bytes) *dev_bytes = w->dev;
     if (device) *device = w->device;
     return QMM_OK;
+}
+
+QMM_API int qmm_checksum_dev(const void* data_dev, size_t len, void* stream, unsigned long long* out) {
+    if (!out || (!data_dev && len)) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if ((uintptr_t)data_dev & 3) return fail(QMM_ERR_INVALID_INPUT, "misaligned pointer (4 B)");
+    if (current_device() < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    cudaStream_t st = (cudaStream_t)stream;
+    // one accumulator per device (the module's __device__ variable); calls are serialised
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    void* acc = nullptr;
+    QMM_CUDA(cudaGetSymbolAddress(&acc, g_qmm_checksum_acc));
+    QMM_CUDA(cudaMemsetAsync(acc, 0, sizeof(unsigned long long), st));
+    if (len) QMM_CUDA(launch_checksum(static_cast<const uint8_t*>(data_dev), len, static_cast<unsigned long long*>(acc), st));
+    unsigned long long v = 0;
+    QMM_CUDA(cudaMemcpyAsync(&v, acc, sizeof v, cudaMemcpyDeviceToHost, st));
+    QMM_CUDA(cudaStreamSynchronize(st));
+    *out = v;
+    return QMM_OK;
+}
+
+QMM_API int qmm_weight_checksum(const qmm_weight* w, unsigned long long* out) {
+    if (!w || !out) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    DeviceGuard guard(w->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    return qmm_checksum_dev(w->dev, w->len, nullptr, out);
 }
 
 QMM_API size_t qmm_workspace_size(int dtype, int act, size_t m, size_t n, size_t k) {
@@ -494,6 +631,7 @@ QMM_API int qmm_matmul_dev(int dtype, int act, const float* x_dev, const uint8_t
 QMM_API int qmm_linear_forward(const qmm_weight* w, const float* x_dev, size_t m, float* y_dev, int act,
                                void* stream) {
     if (!w || !x_dev || !y_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (w->gate_hidden) return fail(QMM_ERR_INVALID_INPUT, "gate/up weight: use qmm_gated_forward");
     if (act != QMM_ACT_F32 && act != QMM_ACT_Q8_0) return fail(QMM_ERR_INVALID_INPUT, "bad activation mode");
     if (m == 0) return QMM_OK;
     DeviceGuard guard(w->device);
@@ -509,6 +647,7 @@ QMM_API int qmm_linear_forward(const qmm_weight* w, const float* x_dev, size_t m
 QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, size_t m, float* y_host, int act,
                                     void* stream) {
     if (!w || !x_host || !y_host) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (w->gate_hidden) return fail(QMM_ERR_INVALID_INPUT, "gate/up weight: use qmm_gated_forward");
     if (act != QMM_ACT_F32 && act != QMM_ACT_Q8_0) return fail(QMM_ERR_INVALID_INPUT, "bad activation mode");
     if (m == 0) return QMM_OK;
     DeviceGuard guard(w->device);
@@ -646,6 +785,19 @@ QMM_API int qmm_dequantize_dev(int dtype, const uint8_t* w_dev, size_t w_len, si
     if (w_len < n_elements / QK * block_bytes(dtype)) return fail(QMM_ERR_SHAPE_MISMATCH, "buffer too short");
     cudaError_t e = launch_dequantize(dtype, w_dev, (int64_t)n_elements, out_dev, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "dequantize");
+    return QMM_OK;
+}
+
+QMM_API int qmm_gated_act_dev(int act_fn, const float* gate_dev, const float* up_dev, size_t m, size_t hidden,
+                              size_t ld, float* out_dev, void* stream) {
+    if (act_fn != QMM_GELU && act_fn != QMM_SILU && act_fn != QMM_RELU)
+        return fail(QMM_ERR_INVALID_INPUT, "unknown activation");
+    if (m * hidden == 0) return QMM_OK;
+    if (!gate_dev || !out_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (ld < hidden) return fail(QMM_ERR_SHAPE_MISMATCH, "row stride below hidden");
+    cudaError_t e = launch_gated_act(act_fn, gate_dev, up_dev, (int64_t)m, (int64_t)hidden, (int64_t)ld, out_dev,
+                                     (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gated activation");
     return QMM_OK;
 }
 

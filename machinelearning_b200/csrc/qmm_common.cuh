@@ -158,6 +158,22 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- activations ------------------------------------------------------------------
+// The reference's element-wise activations in f32, the same operations in the
+// same order: kind 0 tanh-approximated GELU (reference
+// main/features/tensor/src/core/tensor/math.rs:470-475), 1 SiLU (:478-483),
+// 2 ReLU (:465-467).
+__device__ __forceinline__ float act_value(int kind, float g) {
+    if (kind == 0) {
+        const float k = sqrtf(2.0f / 3.14159265358979323846f);
+        return 0.5f * g * (1.0f + tanhf(k * (g + 0.044715f * (g * g * g))));
+    }
+    if (kind == 1) return g * (1.0f / (1.0f + expf(-g)));
+    return fmaxf(g, 0.0f);
+}
+// act(g) * u: the gated forms (GeGLU, SwiGLU) of feed_forward.rs:198-231.
+__device__ __forceinline__ float gated_value(int kind, float g, float u) { return act_value(kind, g) * u; }
+
 // ---- shared loads ----------------------------------------------------------------
 // Plain C++ loads (not asm volatile) so the compiler can schedule them; they
 // stay after an mbarrier wait because the wait's asm clobbers "memory".

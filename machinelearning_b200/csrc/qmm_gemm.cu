@@ -76,6 +76,9 @@ struct GArgs {
     float* y;
     int M, N, K, ksteps, weights_immutable;
     int* err;
+    int gact;        // >= 0: gate/up epilogue (GatedOut), y unused
+    float* gout;     // [M][ghidden]
+    int64_t ghidden;
 };
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -471,9 +474,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         }
         tc_fence_before();
         asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");  // the staging tile is complete
+        if (a.gact >= 0) {
+            // gate/up weight: tile columns [32j, 32j + 16) are gate rows
+            // n0 / 2 + 16j + [0, 16), the next 16 columns the matching up rows;
+            // lanes 0-15 each produce four consecutive outputs
+            const int c = 32 * (lane >> 2) + 4 * (lane & 3);
+            const int64_t i0 = (int64_t)(n0 / 2) + 16 * (lane >> 2) + 4 * (lane & 3);
+            const bool gvec = ((reinterpret_cast<uintptr_t>(a.gout) & 15) == 0) && (a.ghidden % 4 == 0);
+            for (int r = warp - 2; r < T * BM && acc_ok && lane < 16; r += kDqWarps) {
+                const int m = m0 + r;
+                if (m >= a.M) break;
+                const float sc = a.xs[m];
+                const float4 gv = *reinterpret_cast<const float4*>(ys + r * YP + c);
+                const float4 uv = *reinterpret_cast<const float4*>(ys + r * YP + c + 16);
+                const float o0 = gated_value(a.gact, gv.x * sc, uv.x * sc);
+                const float o1 = gated_value(a.gact, gv.y * sc, uv.y * sc);
+                const float o2 = gated_value(a.gact, gv.z * sc, uv.z * sc);
+                const float o3 = gated_value(a.gact, gv.w * sc, uv.w * sc);
+                float* orow = a.gout + (int64_t)m * a.ghidden + i0;
+                if (gvec && i0 + 3 < a.ghidden) {
+                    *reinterpret_cast<float4*>(orow) = make_float4(o0, o1, o2, o3);
+                } else {
+                    if (i0 < a.ghidden) orow[0] = o0;
+                    if (i0 + 1 < a.ghidden) orow[1] = o1;
+                    if (i0 + 2 < a.ghidden) orow[2] = o2;
+                    if (i0 + 3 < a.ghidden) orow[3] = o3;
+                }
+            }
+        }
         const bool vec = ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) && (a.N % 4 == 0);
         const int n = n0 + 4 * lane;
-        for (int r = warp - 2; r < T * BM && acc_ok; r += kDqWarps) {
+        for (int r = warp - 2; r < T * BM && acc_ok && a.gact < 0; r += kDqWarps) {
             const int m = m0 + r;
             if (m >= a.M) break;  // rows are in increasing order
             const float sc = a.xs[m];
@@ -534,7 +565,7 @@ bool gemm_supported(int qt, bool native, int M, int N, int K) {
 size_t gemm_workspace_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((size_t)M * 4); }
 
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws, int* err,
-                        cudaStream_t st, bool weights_immutable) {
+                        cudaStream_t st, bool weights_immutable, const GatedOut& g) {
     __half* x16 = static_cast<__half*>(ws);
     float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256((size_t)M * K * 2));
     {
@@ -558,6 +589,9 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     a.ksteps = (K + BK - 1) / BK;
     a.weights_immutable = weights_immutable ? 1 : 0;
     a.err = err;
+    a.gact = g.act;
+    a.gout = g.out;
+    a.ghidden = g.hidden;
     // two token tiles per CTA once M needs more than one: each dequantised
     // weight tile then feeds twice the tensor work
     const int T = M > BM ? 2 : 1;

@@ -69,6 +69,9 @@ struct Args {
     unsigned* counters;
     int M, N, nb, row_bytes, ks, nbu, kc, pitch, units, weights_immutable, sw;
     int* err;
+    int gact;        // >= 0: gate/up epilogue (GatedOut), y unused
+    float* gout;     // [M][ghidden]
+    int64_t ghidden;
 };
 
 // Sequential activation cursor of one unit: each load advances one block.
@@ -298,9 +301,24 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         }
         if (!ok) break;
         // ------------------------------- epilogue -------------------------------------
+        // A gate/up weight (a.gact >= 0): rows row0 + {0, 8} are gate rows
+        // tile * 16 + g + {0, 8}, rows row0 + {16, 24} the matching up rows.
+        const bool gated = a.gact >= 0;
+        if (gated && a.ks == 1) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int m = nt * 8 + 2 * t + (e & 1);
+                    const int64_t i = (int64_t)tile * kGateGroup + g + ((e & 2) ? 8 : 0);
+                    if (m < a.M && i < a.ghidden)
+                        a.gout[(int64_t)m * a.ghidden + i] = gated_value(a.gact, acc[0][nt][e], acc[1][nt][e]);
+                }
+            }
+        }
         float* dst = a.ks == 1 ? a.y : a.partial + (int64_t)ksi * a.M * a.N;
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < 2 && !(gated && a.ks == 1); ++r) {
             const int ra = row0 + 16 * r, rc = ra + 8;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
@@ -324,8 +342,28 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             if (ticket == (unsigned)(a.ks - 1)) {
                 __threadfence();
                 // the last split sums all partials of this tile in split order
+                if (gated) {
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
+                    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int m = nt * 8 + 2 * t + (e & 1);
+                            const int row = row0 + ((e & 2) ? 8 : 0);
+                            const int64_t i = (int64_t)tile * kGateGroup + g + ((e & 2) ? 8 : 0);
+                            if (m < a.M && i < a.ghidden) {
+                                float s = 0.0f, su = 0.0f;
+                                for (int k = 0; k < a.ks; ++k) {
+                                    const float* pk = a.partial + ((int64_t)k * a.M + m) * a.N + row;
+                                    s += __ldcg(pk);
+                                    su += __ldcg(pk + kGateGroup);
+                                }
+                                a.gout[(int64_t)m * a.ghidden + i] = gated_value(a.gact, s, su);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < 2 && !gated; ++r) {
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -635,13 +673,13 @@ void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws) {
 }
 
 cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvWorkspace& ws,
-                        int* err, cudaStream_t st, bool no_host_alloc) {
+                        int* err, cudaStream_t st, bool no_host_alloc, const GatedOut& g) {
     cudaError_t e;
     if (p.kind == kGemvResident) {
         CUtensorMap tmap;
         e = no_host_alloc ? weight_tensor_map_uncached(w, p, &tmap) : weight_tensor_map(w, p, &tmap);
         if (e != cudaSuccess) return e;
-        return launch_gemv_resident(p, tmap, x, y, err, st, no_host_alloc);
+        return launch_gemv_resident(p, tmap, x, y, err, st, no_host_alloc, g);
     }
     const int nzero = ws.counters ? (p.N + kRows - 1) / kRows : 0;
     if (p.native) {
@@ -680,6 +718,9 @@ cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, flo
     a.pitch = p.pitch;
     a.units = p.units;
     a.err = err;
+    a.gact = g.act;
+    a.gout = g.out;
+    a.ghidden = g.hidden;
     void* args[] = {(void*)&a};
     return launch_pdl_kernel(fn, dim3(p.grid), dim3(kThreads), p.smem, st, args);
 }

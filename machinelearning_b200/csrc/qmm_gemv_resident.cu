@@ -40,6 +40,9 @@ struct RArgs {
     float* y;
     int M, N, K, nb, row_bytes, pitch, cluster, tw, gpc, weights_immutable;
     int* err;
+    int gact;        // >= 0: gate/up epilogue (GatedOut), y unused
+    float* gout;     // [M][ghidden]
+    int64_t ghidden;
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -311,28 +314,48 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
     __syncthreads();
 
     // ---- CTA sums (warp order), then cluster sums (rank order) -------------------------
+    // A gate/up weight (a.gact >= 0) holds gate rows in the first kGateGroup
+    // rows of each tile and the matching up rows in the rest: one thread sums
+    // both and writes act(gate) * up.
     float* cpart = reinterpret_cast<float*>(smem + L.cpart);  // [tw][MP][32 rows]
-    const int nout = ntl * a.M * kRows;  // row fastest: coalesced stores of y
-    for (int o = threadIdx.x; o < nout; o += kThreads) {
-        const int row = o % kRows, m = (o / kRows) % a.M, tl2 = o / (kRows * a.M);
-        float s = 0.0f;
-        for (int q = 0; q < wpt; ++q) s += part[(((tl2 * wpt + q) * NT + (m >> 3)) * kRows + row) * 8 + (m & 7)];
-        if (a.cluster == 1) {
+    const bool gated = a.gact >= 0;
+    const int orows = gated ? kGateGroup : kRows;
+    const int nout = ntl * a.M * orows;  // row fastest: coalesced stores of y
+    auto store = [&](int tl2, int m, int row, float s, float su) {
+        if (gated) {
+            const int64_t i = (int64_t)(tile0 + tl2) * kGateGroup + row;
+            if (i < a.ghidden) a.gout[(int64_t)m * a.ghidden + i] = gated_value(a.gact, s, su);
+        } else {
             const int n = (tile0 + tl2) * kRows + row;
             if (n < a.N) a.y[(int64_t)m * a.N + n] = s;
+        }
+    };
+    for (int o = threadIdx.x; o < nout; o += kThreads) {
+        const int row = o % orows, m = (o / orows) % a.M, tl2 = o / (orows * a.M);
+        float s = 0.0f, su = 0.0f;
+        for (int q = 0; q < wpt; ++q) {
+            const float* pp = part + (((tl2 * wpt + q) * NT + (m >> 3)) * kRows + row) * 8 + (m & 7);
+            s += pp[0];
+            if (gated) su += pp[kGateGroup * 8];
+        }
+        if (a.cluster == 1) {
+            store(tl2, m, row, s, su);
         } else {
             cpart[(tl2 * MP + m) * kRows + row] = s;
+            if (gated) cpart[(tl2 * MP + m) * kRows + row + kGateGroup] = su;
         }
     }
     if (a.cluster > 1) {
         cluster_sync();
         for (int o = rank * kThreads + threadIdx.x; o < nout; o += a.cluster * kThreads) {
-            const int row = o % kRows, m = (o / kRows) % a.M, tl2 = o / (kRows * a.M);
+            const int row = o % orows, m = (o / orows) % a.M, tl2 = o / (orows * a.M);
             const float* src = cpart + (tl2 * MP + m) * kRows + row;
-            float s = 0.0f;
-            for (int q = 0; q < a.cluster; ++q) s += ld_cluster_f32(src, (uint32_t)q);
-            const int n = (tile0 + tl2) * kRows + row;
-            if (n < a.N) a.y[(int64_t)m * a.N + n] = s;
+            float s = 0.0f, su = 0.0f;
+            for (int q = 0; q < a.cluster; ++q) {
+                s += ld_cluster_f32(src, (uint32_t)q);
+                if (gated) su += ld_cluster_f32(src + kGateGroup, (uint32_t)q);
+            }
+            store(tl2, m, row, s, su);
         }
         cluster_sync();  // no CTA leaves while its partials may still be read
     }
@@ -407,7 +430,7 @@ int resident_capacity(int qt, int loader, int nt, int cluster, size_t smem) {
 }
 
 cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,
-                                 cudaStream_t st, bool no_host_alloc) {
+                                 cudaStream_t st, bool no_host_alloc, const GatedOut& g) {
     if (p.native || p.nt > 2 || p.loader == kLoaderCpAsync) return cudaErrorInvalidValue;
     const void* fn = resident_kernel_for(p);
     cudaError_t e = no_host_alloc ? cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem)
@@ -428,6 +451,9 @@ cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, con
     a.gpc = p.gpc;
     a.weights_immutable = p.weights_immutable ? 1 : 0;
     a.err = err;
+    a.gact = g.act;
+    a.gout = g.out;
+    a.ghidden = g.hidden;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kThreads);

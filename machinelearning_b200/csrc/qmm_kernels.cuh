@@ -9,12 +9,31 @@
 
 namespace qmm {
 
+// Rows of a gate/up weight are interleaved in groups of kGateGroup: fused
+// rows [2G*j, 2G*j + G) are gate rows [G*j, G*j + G) and the next G rows the
+// matching up rows, so every 32-row output tile holds whole pairs.
+constexpr int kGateGroup = 16;
+
+// Epilogue of a gate/up matmul: instead of y, out[m][i] = act(y[m][gate i]) *
+// y[m][up i] for i < hidden (act 0 GELU, 1 SiLU). act < 0: plain y.
+struct GatedOut {
+    int act = -1;
+    float* out = nullptr;
+    int64_t hidden = 0;
+};
+
 // ---- quantisers / dequantiser (qmm_quant.cu) -----------------------------------
 cudaError_t launch_quantize_q8_0(const float* x, int64_t n, uint8_t* out, float* scales, bool rounded_inv,
                                  cudaStream_t st);
 cudaError_t launch_quantize_q4_0(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
 cudaError_t launch_quantize_q4_1(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
 cudaError_t launch_dequantize(int qt, const uint8_t* w, int64_t n, float* out, cudaStream_t st);
+// Adds the position-weighted checksum of [p, p + len) into *acc (p 4-byte aligned).
+cudaError_t launch_checksum(const uint8_t* p, uint64_t len, unsigned long long* acc, cudaStream_t st);
+// out[m][i] = act(gate[m*ld + i]) * up[m*ld + i] (up null: act alone);
+// kind 0 = tanh GELU, 1 = SiLU, 2 = ReLU.
+cudaError_t launch_gated_act(int kind, const float* gate, const float* up, int64_t m, int64_t hidden, int64_t ld,
+                             float* out, cudaStream_t st);
 
 // ---- GEMV activation preparation (qmm_quant.cu) ----------------------------------
 // f32 mode:   xf [nb][M][4][16 halves];  native: xq [nb][M][4][8 bytes]
@@ -102,12 +121,13 @@ size_t gemv_workspace_bytes(const GemvPlan& p);
 void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws);
 
 // no_host_alloc: skip the host-side caches (for the allocation-free entry point).
+// g: optional gate/up epilogue (y may then be null).
 cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvWorkspace& ws,
-                        int* err, cudaStream_t st, bool no_host_alloc = false);
+                        int* err, cudaStream_t st, bool no_host_alloc = false, const GatedOut& g = GatedOut());
 
 // The resident kernel (launch_gemv dispatches to it for kGemvResident plans).
 cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,
-                                 cudaStream_t st, bool no_host_alloc);
+                                 cudaStream_t st, bool no_host_alloc, const GatedOut& g);
 
 // Activation-prep tasks ((block, token) pairs) a resident CTA handles per pass:
 // 32 eight-lane groups x this many rounds, loads of a pass in flight together.
@@ -136,7 +156,7 @@ bool gemm_supported(int qt, bool native, int M, int N, int K);
 size_t gemm_workspace_bytes(int M, int K);
 // ws: gemm_workspace_bytes(M, K) bytes, 256-byte aligned.
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
-                        int* err, cudaStream_t st, bool weights_immutable);
+                        int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut());
 
 int* device_error_word(int device);
 

@@ -153,6 +153,43 @@ __global__ void dequantize_kernel(int qt, const uint8_t* __restrict__ w, int64_t
     }
 }
 
+// out[m][i] = act(gate[m * ld + i]) * up[m * ld + i] (up null: act alone), the
+// activation step of the reference's FeedForward::forward
+// (layers/main/src/core/feed_forward.rs:198-251).
+__global__ void gated_act_kernel(int kind, const float* __restrict__ gate, const float* __restrict__ up, int64_t m,
+                                 int64_t hidden, int64_t ld, float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();  // gate / up are written by the matmul before this launch
+    const int64_t total = m * hidden;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t o = (i / hidden) * ld + i % hidden;
+        const float a = act_value(kind, gate[o]);
+        out[i] = up ? a * up[o] : a;
+    }
+}
+
+// Position-weighted checksum of a byte range: sum over its little-endian
+// 32-bit words w_i (tail zero-padded) of w_i * (2i + 1) mod 2^64, added into
+// *acc. Addition mod 2^64 is order independent, so the atomics give one
+// deterministic value. `p` is 4-byte aligned.
+__global__ void checksum_kernel(const uint8_t* __restrict__ p, uint64_t len, unsigned long long* acc) {
+    const uint64_t nfull = len / 4;
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(p);
+    unsigned long long s = 0;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nfull; i += stride)
+        s += (unsigned long long)w[i] * (2ull * i + 1ull);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && (len & 3)) {
+        uint32_t last = 0;
+        for (uint64_t b = nfull * 4; b < len; ++b) last |= (uint32_t)p[b] << (8 * (b - nfull * 4));
+        s += (unsigned long long)last * (2ull * nfull + 1ull);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(acc, s);
+}
+
 // ---- GEMV activation preparation ---------------------------------------------------
 //
 // f32-activation mode: the GEMV feeds x to f16 tensor-core MMAs. Per (token,
@@ -315,6 +352,24 @@ cudaError_t launch_quantize_q4_1(const float* x, int64_t n, uint8_t* out, cudaSt
     note_launch();
     return cudaGetLastError();
 }
+cudaError_t launch_gated_act(int kind, const float* gate, const float* up, int64_t m, int64_t hidden, int64_t ld,
+                             float* out, cudaStream_t st) {
+    if (m * hidden == 0) return cudaSuccess;
+    int64_t g = (m * hidden + 255) / 256;
+    if (g > 148 * 8) g = 148 * 8;
+    void* args[] = {(void*)&kind, (void*)&gate, (void*)&up, (void*)&m, (void*)&hidden, (void*)&ld, (void*)&out};
+    return launch_pdl_kernel((const void*)gated_act_kernel, dim3((unsigned)g), dim3(256), 0, st, args);
+}
+
+cudaError_t launch_checksum(const uint8_t* p, uint64_t len, unsigned long long* acc, cudaStream_t st) {
+    uint64_t g = (len / 4 + 255) / 256;
+    if (g < 1) g = 1;
+    if (g > 148 * 16) g = 148 * 16;
+    checksum_kernel<<<(int)g, 256, 0, st>>>(p, len, acc);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t launch_dequantize(int qt, const uint8_t* w, int64_t n, float* out, cudaStream_t st) {
     if (n == 0) return cudaSuccess;
     int64_t g = (n + 255) / 256;

@@ -25,6 +25,7 @@ class QuantWeight:
     def __init__(self, handle: int, dtype: int, n: int, k: int, device: int):
         self._h = ctypes.c_void_p(handle)
         self.dtype, self.n, self.k, self.device = dtype, n, k, device
+        self.gate_hidden = 0  # > 0: a gate/up weight (machinelearning_b200.fused.fuse_gate_up)
 
     @classmethod
     def from_host(cls, dtype: int, n: int, k: int, data, device: int = 0) -> "QuantWeight":

@@ -251,3 +251,50 @@ MATMUL = {
     (Q4_1, False): matmul_f32_q4_1,
     (Q4_1, True): matmul_f32_q4_1_native,
 }
+
+
+# ---- activations and fused projections (layers crate) ------------------------------
+# Element-wise in float32, the reference's operations in its order
+# (main/features/tensor/src/core/tensor/math.rs:465-483); numpy's float32
+# tanh / exp stand in for Rust's f32 tanh / exp (libm), which round differently
+# by an ulp or so.
+def gelu(x) -> np.ndarray:
+    """math.rs:470-475: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))."""
+    x = _f32(x)
+    k = np.sqrt(np.float32(2.0) / np.float32(np.pi), dtype=np.float32)
+    with np.errstate(over="ignore"):
+        return (np.float32(0.5) * x * (np.float32(1.0) + np.tanh(k * (x + np.float32(0.044715) * (x * x * x))))).astype(np.float32)
+
+
+def silu(x) -> np.ndarray:
+    """math.rs:478-483: x * (1 / (1 + exp(-x)))."""
+    x = _f32(x)
+    with np.errstate(over="ignore"):
+        return (x * (np.float32(1.0) / (np.float32(1.0) + np.exp(-x)))).astype(np.float32)
+
+
+def relu(x) -> np.ndarray:
+    """math.rs:465-467: x.max(0)."""
+    return np.maximum(_f32(x), np.float32(0.0))
+
+
+ACTIVATIONS = {0: gelu, 1: silu, 2: relu}
+
+
+def fuse_rows(*parts) -> np.ndarray:
+    """Byte concatenation of weights with equal in_features, as
+    Attention::fuse_qkv_weights (layers/main/src/core/attention.rs:306-339) and
+    FeedForward::fuse_gate_up_weights (feed_forward.rs:147-187) build the fused
+    tensor: the fused matmul's output row is the parts' outputs side by side."""
+    return np.concatenate([_u8(p) for p in parts])
+
+
+def gated_ffn_hidden(act: int, x, gate_w, up_w, dtype: int, m: int, k: int, hidden: int) -> np.ndarray:
+    """The hidden activation of FeedForward::forward's gated branch
+    (feed_forward.rs:198-231, fused or not: both give the same rows):
+    act(matmul(x, gate)) * matmul(x, up) with the f32-activation matmul of the
+    weight's type (the fused Linear has use_native_* false)."""
+    mm = MATMUL[(dtype, False)]
+    g = mm(x, gate_w, m, k, hidden)
+    u = mm(x, up_w, m, k, hidden)
+    return (ACTIVATIONS[act](g) * u).astype(np.float32)

@@ -534,6 +534,84 @@ bool resident_plan(GemvPlan& q, int num_sms) {
     return true;
 }
 
+// The band kernel (M <= 8, f32 activations, 16-byte row pitch), for weights
+// the resident kernel cannot hold. K is cut into ks slices of q chunks of kc
+// blocks (slice and chunk starts multiples of 8 blocks, 4 for Q4_1: 16-byte
+// aligned TMA coordinates); a chunk is one 2-D box of 32 rows whose width is
+// padded to a row pitch of 4 mod 8 words and kept within 1 KB (B200, measured:
+// 32-row boxes of 0.6 to 1 KB rows stream at ~5.7 TB/s through a 3-6 stage
+// ring). The activations of a slice live in shared memory; the ring takes
+// what they and the partial tiles leave (3 to 8 stages). Among the fitting
+// choices: the shortest stream per CTA (its tiles times its slice's boxes),
+// each box costing its bytes but at least kBandBoxFloor byte-times (a box
+// takes ~360 ns of an SM's TMA at least, ~14 KB at its share of HBM
+// bandwidth: 32-row boxes of 288-byte rows stream at only ~3.8 TB/s), then
+// the smaller ks (fewer partial sums in global memory).
+constexpr int kBandW = 8;  // consumer warps per CTA
+// Token counts routed to the band kernel (measured faster than the streaming
+// kernel at M = 1; larger M stay on the streaming kernel for now).
+constexpr int kBandMaxM = 1;
+constexpr double kBandBoxFloor = 14000.0;
+constexpr size_t kBandSmemMax = 227 * 1024;
+
+bool band_plan(GemvPlan& q, int num_sms) {
+    if (q.native || q.M > kBandMaxM || q.row_bytes % 16 != 0) return false;
+    const int bb = block_bytes(q.qt);
+    const int align = q.qt == kQ4_1 ? 4 : 8;
+    const int tiles = (q.N + kRows - 1) / kRows;
+    double best = 0.0;
+    bool found = false;
+    for (int ks = 1; ks <= 8; ks *= 2) {
+        const int target = (q.nb + ks - 1) / ks;
+        const int qmin = (target * bb + 1007) / 1008;
+        for (int nq = qmin; nq <= qmin + 4; ++nq) {
+            const int kc = ((target + nq - 1) / nq + align - 1) / align * align;
+            int pitch = (kc * bb + 15) / 16 * 16;
+            if (((pitch / 4) & 7) != 4) pitch += 16;
+            if (pitch > 1024) continue;
+            const int nbs = nq * kc;
+            if (ks > 1 && (long)nbs * (ks - 1) >= q.nb) continue;  // a slice without blocks
+            const size_t fixed = band_layout(0, pitch, nbs, q.M, kBandW).total;
+            if (fixed + 3 * 32 * (size_t)pitch > kBandSmemMax) continue;
+            int S = (int)((kBandSmemMax - fixed) / (32 * (size_t)pitch));
+            if (S > 8) S = 8;
+            const size_t smem = band_layout(S, pitch, nbs, q.M, kBandW).total;
+            int cap = band_capacity(q.qt, kBandW, q.M, smem);
+            if (cap <= 0) cap = num_sms;
+            long grid = cap < (long)tiles * ks ? cap : (long)tiles * ks;
+            grid -= grid % ks;
+            if (grid < ks) continue;
+            const long per_slice = grid / ks;
+            const long rounds = (tiles + per_slice - 1) / per_slice;
+            const int nch = ks == 1 ? (q.nb + kc - 1) / kc : nq;  // chunks of the longest slice
+            const double boxes = (double)rounds * nch;
+            const double bytes = boxes * 32.0 * pitch;
+            // shallow rings lose bandwidth (measured: 3 stages ~13% below 6)
+            const double depth = S >= 5 ? 1.0 : (S == 4 ? 1.05 : 1.13);
+            const double cost =
+                (bytes > boxes * kBandBoxFloor ? bytes : boxes * kBandBoxFloor) * depth * (ks > 1 ? 1.02 : 1.0);
+            if (!found || cost < best) {
+                found = true;
+                best = cost;
+                q.ks = ks;
+                q.nbu = nbs;
+                q.kc = kc;
+                q.pitch = pitch;
+                q.sw = S;
+                q.smem = smem;
+                q.grid = (int)grid;
+            }
+        }
+    }
+    if (!found) return false;
+    q.kind = kGemvBand;
+    q.tw = kBandW;
+    q.cluster = 1;
+    q.loader = kLoaderTma2d;
+    q.units = 0;
+    return true;
+}
+
 }  // namespace
 
 cudaError_t encode_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t dim0,
@@ -551,18 +629,31 @@ cudaError_t encode_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const voi
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t set_max_dynamic_smem(const void* fn) {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, fn);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+}
+
 cudaError_t ensure_dynamic_smem(const void* fn, size_t bytes) {
     static std::mutex mu;
-    static std::map<std::pair<int, const void*>, size_t> done;
+    static std::map<std::pair<int, const void*>, bool> done;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(mu);
-    size_t& have = done[{dev, fn}];
-    if (have >= bytes) return cudaSuccess;
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-    if (e == cudaSuccess) have = bytes;
-    return e;
+    bool& d = done[{dev, fn}];
+    if (!d) {
+        e = set_max_dynamic_smem(fn);
+        if (e != cudaSuccess) return e;
+        d = true;
+    }
+    (void)bytes;  // larger than the device allows: the launch reports it
+    return cudaSuccess;
 }
 
 bool gemv_plan(int qt, bool native, int M, int N, int K, int num_sms, GemvPlan* p) {
@@ -601,6 +692,13 @@ bool gemv_plan(int qt, bool native, int M, int N, int K, int num_sms, GemvPlan* 
     if (resident_plan(q, num_sms)) {
         *p = q;
         return true;
+    }
+    {
+        GemvPlan b = q;
+        if (band_plan(b, num_sms)) {
+            *p = b;
+            return true;
+        }
     }
     q.kind = kGemvStreaming;
     // Shared memory and L1 share one array per SM. The activation fragments are
@@ -646,6 +744,10 @@ bool gemv_plan(int qt, bool native, int M, int N, int K, int num_sms, GemvPlan* 
 
 size_t gemv_workspace_bytes(const GemvPlan& p) {
     if (p.kind == kGemvResident) return 0;  // everything lives in shared memory
+    if (p.kind == kGemvBand)  // slice partials and tickets when K is split
+        return p.ks > 1 ? align256((size_t)p.ks * p.M * p.N * sizeof(float)) +
+                              align256((size_t)((p.N + kRows - 1) / kRows) * sizeof(unsigned))
+                        : 0;
     const size_t Mpad = (size_t)token_pad(p.M);
     size_t s = align256((size_t)p.nb * p.M * (p.native ? 32 : 128));
     s += align256((size_t)p.nb * Mpad * 16);  // side records: (Mpad/2) x 32 B per block
@@ -661,6 +763,13 @@ void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws) {
     uint8_t* c = static_cast<uint8_t*>(base);
     *ws = GemvWorkspace{};
     if (p.kind == kGemvResident) return;
+    if (p.kind == kGemvBand) {
+        if (p.ks > 1) {
+            ws->partial = reinterpret_cast<float*>(c);
+            ws->counters = reinterpret_cast<unsigned*>(c + align256((size_t)p.ks * p.M * p.N * sizeof(float)));
+        }
+        return;
+    }
     ws->xa = c;
     c += align256((size_t)p.nb * p.M * (p.native ? 32 : 128));
     ws->side = reinterpret_cast<uint32_t*>(c);
@@ -675,6 +784,12 @@ void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws) {
 cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvWorkspace& ws,
                         int* err, cudaStream_t st, bool no_host_alloc, const GatedOut& g) {
     cudaError_t e;
+    if (p.kind == kGemvBand) {
+        CUtensorMap tmap;
+        e = no_host_alloc ? weight_tensor_map_uncached(w, p, &tmap) : weight_tensor_map(w, p, &tmap);
+        if (e != cudaSuccess) return e;
+        return launch_gemv_band(p, tmap, x, y, ws, err, st, no_host_alloc, g);
+    }
     if (p.kind == kGemvResident) {
         CUtensorMap tmap;
         e = no_host_alloc ? weight_tensor_map_uncached(w, p, &tmap) : weight_tensor_map(w, p, &tmap);
@@ -691,8 +806,7 @@ cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, flo
     const void* fn = kernel_for(p);
     // no_host_alloc: set the attribute and encode the tensor map on every call
     // instead of going through the (heap-backed) caches
-    e = no_host_alloc ? cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem)
-                      : ensure_dynamic_smem(fn, p.smem);
+    e = no_host_alloc ? set_max_dynamic_smem(fn) : ensure_dynamic_smem(fn, p.smem);
     if (e != cudaSuccess) return e;
     Args a;
     if (p.loader != kLoaderCpAsync) {

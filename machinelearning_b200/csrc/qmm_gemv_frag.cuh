@@ -187,4 +187,60 @@ __device__ __forceinline__ void consume_group(const uint8_t* r0, const uint8_t* 
     }
 }
 
+// Packed form for up to 4 tokens (f32 activations): the 8 MMA columns carry
+// (token, half) pairs, column 2m the hi half of token m and column 2m + 1 its
+// lo half, so one chain of two MMAs per block covers both halves. Lane (g, t)
+// supplies column g (xb: token g >> 1's hi or lo record) and receives token
+// t's two halves for rows g and g + 8, added into acc[0] / acc[1]. c: the
+// accumulator start of token t's hi column (-corr), s: its scale 2^e, sx:
+// its block sum (Q4_1). Same products and per-block terms as consume_group.
+template <int QT, bool AL>
+__device__ __forceinline__ void consume_group_packed(const uint8_t* r0, const uint8_t* r1, int t, uint4 xb, float c,
+                                                     float s, float sx, float (&acc)[2]) {
+    const float d0 = f16_bits_to_f32((uint16_t)lds_u16(r0));
+    const float d1 = f16_bits_to_f32((uint16_t)lds_u16(r1));
+    constexpr int NOFF = (QT == kQ4_1) ? 4 : 2;
+    uint32_t A0[4], A1[4];
+    if constexpr (QT == kQ8_0) {
+        const uint32_t u00 = ld_word<AL>(r0 + NOFF + 4 * t) ^ 0x80808080u;
+        const uint32_t u01 = ld_word<AL>(r0 + NOFF + 16 + 4 * t) ^ 0x80808080u;
+        const uint32_t u10 = ld_word<AL>(r1 + NOFF + 4 * t) ^ 0x80808080u;
+        const uint32_t u11 = ld_word<AL>(r1 + NOFF + 16 + 4 * t) ^ 0x80808080u;
+        A0[0] = __byte_perm(u00, 0x64646464u, 0x4140);
+        A0[1] = __byte_perm(u10, 0x64646464u, 0x4140);
+        A0[2] = __byte_perm(u00, 0x64646464u, 0x4342);
+        A0[3] = __byte_perm(u10, 0x64646464u, 0x4342);
+        A1[0] = __byte_perm(u01, 0x64646464u, 0x4140);
+        A1[1] = __byte_perm(u11, 0x64646464u, 0x4140);
+        A1[2] = __byte_perm(u01, 0x64646464u, 0x4342);
+        A1[3] = __byte_perm(u11, 0x64646464u, 0x4342);
+    } else {
+        const uint32_t w0 = ld_word<AL>(r0 + NOFF + 4 * t);
+        const uint32_t w1 = ld_word<AL>(r1 + NOFF + 4 * t);
+        const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
+        A0[0] = lop3_and_or(w0, 0x000F000Fu, 0x64006400u);
+        A0[1] = lop3_and_or(w1, 0x000F000Fu, 0x64006400u);
+        A0[2] = lop3_and_or(w0s, 0x000F000Fu, 0x64006400u);
+        A0[3] = lop3_and_or(w1s, 0x000F000Fu, 0x64006400u);
+        A1[0] = lop3_and_or(w0, 0x00F000F0u, 0x64006400u);
+        A1[1] = lop3_and_or(w1, 0x00F000F0u, 0x64006400u);
+        A1[2] = lop3_and_or(w0s, 0x00F000F0u, 0x64006400u);
+        A1[3] = lop3_and_or(w1s, 0x00F000F0u, 0x64006400u);
+    }
+    const float c0[4] = {c, 0.0f, c, 0.0f};
+    float e[4], h[4];
+    mma_f16_c(e, A0, xb.x, xb.y, c0);
+    mma_f16_c(h, A1, xb.z, xb.w, e);
+    const float v0 = h[0] + h[1], v1 = h[2] + h[3];  // hi + lo, rows g and g + 8
+    if constexpr (QT == kQ4_1) {
+        const float m0 = f16_bits_to_f32((uint16_t)lds_u16(r0 + 2));
+        const float m1 = f16_bits_to_f32((uint16_t)lds_u16(r1 + 2));
+        acc[0] = fmaf(s, fmaf(d0, v0, m0 * sx), acc[0]);
+        acc[1] = fmaf(s, fmaf(d1, v1, m1 * sx), acc[1]);
+    } else {
+        acc[0] = fmaf(d0 * s, v0, acc[0]);
+        acc[1] = fmaf(d1 * s, v1, acc[1]);
+    }
+}
+
 }  // namespace qmm

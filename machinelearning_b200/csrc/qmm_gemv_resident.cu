@@ -28,6 +28,7 @@
 
 #include "qmm_common.cuh"
 #include "qmm_gemv_frag.cuh"
+#include "qmm_gemv_xsmem.cuh"
 #include "qmm_kernels.cuh"
 
 namespace qmm {
@@ -44,48 +45,6 @@ struct RArgs {
     float* gout;     // [M][ghidden]
     int64_t ghidden;
 };
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-// Every thread of every CTA of the cluster: release this CTA's shared-memory
-// writes, acquire the others'.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile(
-        "barrier.cluster.arrive.release.aligned;\n\t"
-        "barrier.cluster.wait.acquire.aligned;" ::
-            : "memory");
-}
-// The f32 at the same shared-memory offset as `local` in CTA `rank` of the cluster.
-__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
-    uint32_t ra;
-    float v;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
-
-// 2^n as an exact f32 for n in [-127, 127] (2^-127 is subnormal).
-__device__ __forceinline__ float exp2_int(int n) {
-    return n >= -126 ? __int_as_float((n + 127) << 23) : __int_as_float(0x00400000);
-}
-// The exponent E with a = f * 2^E, f in [0.5, 1), for finite a > 0 (the
-// exponent frexpf returns), read from the bits.
-__device__ __forceinline__ int frexp_exponent(float a) {
-    const int bits = __float_as_int(a);
-    const int biased = bits >> 23;
-    if (biased != 0) return biased - 126;
-    return (31 - __clz(bits)) - 148;  // subnormal: highest set mantissa bit
-}
 
 template <int QT, int NT, int LOADER>
 __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid_constant__ RArgs a) {
@@ -142,103 +101,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
     // the MMA adds, s = 2^e, sx = block sum (Q4_1). Layout and element order
     // as written by xprep_f32_kernel.
     const uint32_t lo_plane = (uint32_t)a.gpc * kChunk * a.M * 64;  // bytes from the hi to the lo plane
-    {
-        uint8_t* xf = smem + L.xf;
-        uint32_t* side = reinterpret_cast<uint32_t*>(smem + L.side);
-        const int npt = MP - a.M;  // padding tokens per block: neutral records
-        for (int i = threadIdx.x; i < nbc * npt; i += kThreads) {
-            const int b = i / npt, m = a.M + i % npt;
-            uint32_t* r8 = side + (b * (MP / 2) + (m >> 1)) * 8 + (m & 1);
-            r8[0] = r8[2] = r8[4] = r8[6] = 0u;
-        }
-        const bool x16 = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-        const int ntask = nbc * a.M;
-        const int gl = lane & 7;         // lane in the 8-lane group: elements 4gl..4gl+3
-        const bool upper = gl >= 4;      // elements 16..31
-        // kPrepUnroll rounds of 32 tasks per pass: their global loads are all
-        // in flight together instead of one L2 round trip per round
-        constexpr int kPrepUnroll = kResidentPrepUnroll;
-        constexpr int kRound = kThreads / 8;
-        for (int base = warp * 4; base < ntask; base += kRound * kPrepUnroll) {  // warp-uniform trip count
-          float vu[kPrepUnroll][4];
-#pragma unroll
-          for (int u = 0; u < kPrepUnroll; ++u) {
-            const int task = base + u * kRound + (lane >> 3);
-            vu[u][0] = vu[u][1] = vu[u][2] = vu[u][3] = 0.0f;
-            if (task < ntask) {
-                const int b = task / a.M, m = task % a.M;
-                const float* src = a.x + (int64_t)m * a.K + (int64_t)(kb0 + b) * QK + 4 * gl;
-                if (x16) {
-                    const float4 q = *reinterpret_cast<const float4*>(src);
-                    vu[u][0] = q.x;
-                    vu[u][1] = q.y;
-                    vu[u][2] = q.z;
-                    vu[u][3] = q.w;
-                } else {
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) vu[u][r] = src[r];
-                }
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kPrepUnroll; ++u) {
-            if (base + u * kRound >= ntask) break;  // warp-uniform
-            const int task = base + u * kRound + (lane >> 3);
-            const bool live = task < ntask;
-            const int b = live ? task / a.M : 0;
-            const int m = live ? task % a.M : 0;
-            const float v[4] = {vu[u][0], vu[u][1], vu[u][2], vu[u][3]};
-            float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
-            int e = 0;
-            if (am > 0.0f && am <= 3.402823466e38f) e = max(-126, min(127, frexp_exponent(am) - 14));
-            // Q4 formats: high-nibble elements meet weights pre-multiplied by 16
-            // by the magic trick, so their activations are pre-divided by 16.
-            // Multiplying by an exact power of two rounds exactly as ldexpf.
-            const float scale = exp2_int(-e) * ((QT != kQ8_0 && upper) ? 0.0625f : 1.0f);
-            const float coef = QT == kQ8_0 ? 1152.0f : (QT == kQ4_0 ? (upper ? 1152.0f : 1032.0f) : 1024.0f);
-            // record order inside each group of four: Q8_0 (0,1,2,3), Q4 (0,2,1,3)
-            constexpr int P1 = QT == kQ8_0 ? 1 : 2, P2 = QT == kQ8_0 ? 2 : 1;
-            float vv[4];
-            vv[0] = v[0] * scale;
-            vv[1] = v[P1] * scale;
-            vv[2] = v[P2] * scale;
-            vv[3] = v[3] * scale;
-            const __half2 h01 = __floats2half2_rn(vv[0], vv[1]), h23 = __floats2half2_rn(vv[2], vv[3]);
-            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-            const __half2 l01 = __floats2half2_rn(vv[0] - f01.x, vv[1] - f01.y);
-            const __half2 l23 = __floats2half2_rn(vv[2] - f23.x, vv[3] - f23.y);
-            const float2 g01 = __half22float2(l01), g23 = __half22float2(l23);
-            const float rep[4] = {f01.x + g01.x, f01.y + g01.y, f23.x + g23.x, f23.y + g23.y};
-            float corr = coef * rep[0] + coef * rep[1] + coef * rep[2] + coef * rep[3];
-            float sx = 0.0f;
-            if (QT == kQ4_1) sx = (rep[0] + rep[1] + rep[2] + rep[3]) * (upper ? 16.0f : 1.0f);
-            corr += __shfl_xor_sync(0xffffffffu, corr, 1);
-            corr += __shfl_xor_sync(0xffffffffu, corr, 2);
-            corr += __shfl_xor_sync(0xffffffffu, corr, 4);
-            if (QT == kQ4_1) {
-                sx += __shfl_xor_sync(0xffffffffu, sx, 1);
-                sx += __shfl_xor_sync(0xffffffffu, sx, 2);
-                sx += __shfl_xor_sync(0xffffffffu, sx, 4);
-            }
-            if (live) {
-                // thread t's 16-byte record holds elements 4t..4t+3 then
-                // 16+4t..16+4t+3, in the hi plane and in the lo plane
-                uint8_t* rec = xf + ((uint32_t)(b * a.M + m) * 4 + (gl & 3)) * 16 + (upper ? 8 : 0);
-                *reinterpret_cast<uint2*>(rec) = make_uint2(h2_bits(h01), h2_bits(h23));
-                *reinterpret_cast<uint2*>(rec + lo_plane) = make_uint2(h2_bits(l01), h2_bits(l23));
-                if (gl == 0) {
-                    uint32_t* r8 = side + (b * (MP / 2) + (m >> 1)) * 8 + (m & 1);
-                    r8[0] = r8[2] = __float_as_uint(-corr);  // the MMA accumulator starts at -corr
-                    r8[4] = __float_as_uint(exp2_int(e));
-                    r8[6] = __float_as_uint(sx);
-                }
-            }
-          }
-        }
-    }
+    prep_x_smem<QT>(a.x, a.M, a.K, kb0, nbc, smem + L.xf, lo_plane, reinterpret_cast<uint32_t*>(smem + L.side),
+                    MP / 2, threadIdx.x, kThreads);
     __syncthreads();
     bool ok = true;
     if (ng > 0) {
@@ -403,7 +267,7 @@ int resident_capacity(int qt, int loader, int nt, int cluster, size_t smem) {
         if (e.dev == dev && e.fn == fn && e.cluster == cluster && e.smem == smem) return e.cap;
     }
     int cap = 0;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess) {
+    if (ensure_dynamic_smem(fn, smem) == cudaSuccess) {
         if (cluster == 1) {
             int per_sm = 0, sms = 0;
             if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) == cudaSuccess &&
@@ -433,8 +297,7 @@ cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, con
                                  cudaStream_t st, bool no_host_alloc, const GatedOut& g) {
     if (p.native || p.nt > 2 || p.loader == kLoaderCpAsync) return cudaErrorInvalidValue;
     const void* fn = resident_kernel_for(p);
-    cudaError_t e = no_host_alloc ? cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem)
-                                  : ensure_dynamic_smem(fn, p.smem);
+    cudaError_t e = no_host_alloc ? set_max_dynamic_smem(fn) : ensure_dynamic_smem(fn, p.smem);
     if (e != cudaSuccess) return e;
     RArgs a;
     a.tmap = tmap;

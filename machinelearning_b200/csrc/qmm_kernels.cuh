@@ -52,7 +52,12 @@ cudaError_t launch_pdl_kernel(const void* fn, dim3 grid, dim3 block, size_t smem
 //                 its whole share of the weights into shared memory, prepares
 //                 the activations itself, and K splits are summed on chip
 //                 (warps through shared memory, cluster CTAs through DSMEM).
-enum GemvKind : int { kGemvStreaming = 0, kGemvResident = 1 };
+// kGemvBand:      decode shapes (M <= 8, f32 activations) too large to keep on
+//                 chip: each CTA owns a K slice of a run of 32-row tiles with
+//                 its activations prepared in shared memory, streams the
+//                 weights through a deep ring of wide TMA boxes, and slices are
+//                 summed in slice order by the last to finish (qmm_gemv_band.cu).
+enum GemvKind : int { kGemvStreaming = 0, kGemvResident = 1, kGemvBand = 2 };
 
 struct GemvPlan {
     int kind;        // GemvKind
@@ -105,6 +110,30 @@ __host__ __device__ inline ResidentLayout resident_layout(int tw, int gpc, int p
     return L;
 }
 
+// Shared-memory layout of the band kernel (byte offsets), host and device:
+// S ring stages of 32 rows x pitch, activations of nbs blocks x M tokens
+// (side records for ceil(M / 2) token pairs), W consumer warps.
+struct BandLayout {
+    uint32_t ring, xf, side, part, bar, total;
+};
+__host__ __device__ inline BandLayout band_layout(int S, int pitch, int nbs, int M, int W) {
+    BandLayout L;
+    uint32_t o = 0;
+    L.ring = o;  // [S][32 rows][pitch]
+    o += (uint32_t)S * 32u * (uint32_t)pitch;
+    o = (o + 127u) & ~127u;
+    L.xf = o;  // hi plane [nbs][M][4] x 16 B, then the lo plane
+    o += (uint32_t)nbs * (uint32_t)M * 128u;
+    L.side = o;  // [nbs][ceil(M / 2) pairs] x 32 B
+    o += (uint32_t)nbs * (uint32_t)((M + 1) / 2) * 32u;
+    L.part = o;  // [2 slots][W warps][32 rows][8 tokens] f32
+    o += 2u * (uint32_t)W * 32u * 8u * 4u;
+    L.bar = o;  // full[S], empty[S], rfull[2], rempty[2]
+    o += (uint32_t)(2 * S + 4) * 8u;
+    L.total = o;
+    return L;
+}
+
 // Fills a plan for the given problem on a device with `num_sms` SMs. Returns
 // false if the shape is not handled by the GEMV kernel (M > 64).
 bool gemv_plan(int qt, bool native, int M, int N, int K, int num_sms, GemvPlan* p);
@@ -125,6 +154,16 @@ void gemv_workspace_carve(const GemvPlan& p, void* base, GemvWorkspace* ws);
 cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, float* y, const GemvWorkspace& ws,
                         int* err, cudaStream_t st, bool no_host_alloc = false, const GatedOut& g = GatedOut());
 
+// The band kernel (launch_gemv dispatches kGemvBand plans to it; tmap: the
+// weights with a [pitch / 4, 32] box), threads per CTA for W consumer warps,
+// and how many of its CTAs with `smem` bytes fit on the current device at
+// once (0: unknown).
+cudaError_t launch_gemv_band(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y,
+                             const GemvWorkspace& ws, int* err, cudaStream_t st, bool no_host_alloc,
+                             const GatedOut& g);
+int band_threads(int W);
+int band_capacity(int qt, int W, int M, size_t smem);
+
 // The resident kernel (launch_gemv dispatches to it for kGemvResident plans).
 cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,
                                  cudaStream_t st, bool no_host_alloc, const GatedOut& g);
@@ -139,9 +178,13 @@ constexpr int kResidentPrepUnroll = 8;
 // smem) in a fixed table (no heap use).
 int resident_capacity(int qt, int loader, int nt, int cluster, size_t smem);
 
-// Opts a kernel in to `bytes` of dynamic shared memory on the current device
-// (cached per device and kernel).
+// Opts a kernel in to dynamic shared memory on the current device: the limit
+// is raised once to the device maximum and never lowered, so occupancy
+// queries and launches with any size up to it cannot undo one another
+// (ensure_dynamic_smem caches per device and kernel; set_max_dynamic_smem
+// does the same without the cache's heap use).
 cudaError_t ensure_dynamic_smem(const void* fn, size_t bytes);
+cudaError_t set_max_dynamic_smem(const void* fn);
 
 // A 2-D TMA tensor map (dim0 innermost, in elements; zero fill out of bounds).
 cudaError_t encode_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t dim0,

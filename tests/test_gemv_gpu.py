@@ -253,6 +253,33 @@ def test_resident_kernel_variants(oracle, torch_cuda, qlib, case):
     check(oracle, torch_cuda, qlib, dt, 1, x, w, m, k, n)
 
 
+# Band kernel (M <= 8, f32 activations, 16-byte row pitch, weights above what
+# the resident kernel holds on chip: > ~30 MB): K slices over clusters, ragged
+# last tiles, a shorter last slice, every block type. One launch per call.
+BAND = [
+    (Q4_0, 1, 16384, 4100),  # ragged last tile (4 rows)
+    (Q8_0, 1, 8192, 5000),
+    (Q4_1, 1, 12288, 7000),  # 20-byte blocks
+    (Q8_0, 1, 14336, 4096),
+    (Q4_0, 1, 8448, 9000),   # 264 blocks: the last K slice is shorter
+    (Q4_0, 1, 8192, 28672),  # Llama-70B gate
+]
+
+
+@pytest.mark.parametrize("case", range(len(BAND)))
+def test_band_kernel_variants(oracle, torch_cuda, qlib, case):
+    dt, m, k, n = BAND[case]
+    assert n * (k // 32) * BB[dt] > 32 << 20  # beyond the resident kernel's capacity
+    w = random_blocks(dt, n, k, seed=700 + case)
+    x = np.random.default_rng(750 + case).normal(0, 1, m * k).astype(np.float32)
+    before = qlib.qmm_launch_count()
+    y = gpu_matmul(torch_cuda, qlib, dt, 0, x, w, m, k, n)
+    assert qlib.qmm_launch_count() - before == 1  # one kernel: no separate activation prep
+    assert_close_rel(y, getattr(oracle, ORACLE_FN[(dt, 0)])(x, w, m, k, n))
+    y2 = gpu_matmul(torch_cuda, qlib, dt, 0, x, w, m, k, n)
+    assert_bits_equal(y2, y, "band kernel run to run")
+
+
 def test_resident_kernel_unaligned_activations(oracle, torch_cuda, qlib):
     """x only 4-byte aligned: the in-kernel activation prep uses scalar loads."""
     torch = torch_cuda

@@ -534,78 +534,64 @@ bool resident_plan(GemvPlan& q, int num_sms) {
     return true;
 }
 
-// The band kernel (M <= 8, f32 activations, 16-byte row pitch), for weights
-// the resident kernel cannot hold. K is cut into ks slices of q chunks of kc
-// blocks (slice and chunk starts multiples of 8 blocks, 4 for Q4_1: 16-byte
-// aligned TMA coordinates); a chunk is one 2-D box of 32 rows whose width is
-// padded to a row pitch of 4 mod 8 words and kept within 1 KB (B200, measured:
-// 32-row boxes of 0.6 to 1 KB rows stream at ~5.7 TB/s through a 3-6 stage
-// ring). The activations of a slice live in shared memory; the ring takes
-// what they and the partial tiles leave (3 to 8 stages). Among the fitting
-// choices: the shortest stream per CTA (its tiles times its slice's boxes),
-// each box costing its bytes but at least kBandBoxFloor byte-times (a box
-// takes ~360 ns of an SM's TMA at least, ~14 KB at its share of HBM
-// bandwidth: 32-row boxes of 288-byte rows stream at only ~3.8 TB/s), then
-// the smaller ks (fewer partial sums in global memory).
-constexpr int kBandW = 8;  // consumer warps per CTA
-// Token counts routed to the band kernel (measured faster than the streaming
-// kernel at M = 1; larger M stay on the streaming kernel for now).
-constexpr int kBandMaxM = 1;
-constexpr double kBandBoxFloor = 14000.0;
+// The band kernel (M = 1, f32 activations, 16-byte row pitch), for weights
+// the resident kernel cannot hold. K is cut into ks slices of whole chunks of
+// kc = kBandWarps * band_bpw blocks (a multiple of 8: 16-byte aligned TMA
+// coordinates); a chunk is one 2-D box of 32 rows, its width padded to a row
+// pitch of 4 mod 8 words (B200, measured: 32-row boxes of 0.6 to 1 KB rows
+// stream at ~5.5-5.8 TB/s through a 4-6 stage ring, 288-byte rows at ~3.8).
+// The activations of a slice live in shared memory; the ring takes what they
+// and the partial tiles leave (3 to 8 stages). Among the fitting choices: the
+// shortest stream per CTA (its tiles times its slice's boxes), then the
+// smaller ks (fewer partial sums in global memory).
 constexpr size_t kBandSmemMax = 227 * 1024;
+constexpr int kBandMaxM = 1;  // token counts routed here (band_kernel_m)
 
 bool band_plan(GemvPlan& q, int num_sms) {
     if (q.native || q.M > kBandMaxM || q.row_bytes % 16 != 0) return false;
     const int bb = block_bytes(q.qt);
-    const int align = q.qt == kQ4_1 ? 4 : 8;
+    const int kc = kBandWarps * band_bpw(q.qt);
+    const int mt = band_mt(q.M);
+    int pitch = kc * bb;
+    if (((pitch / 4) & 7) != 4) pitch += 16;
+    if (pitch > 1024) return false;
     const int tiles = (q.N + kRows - 1) / kRows;
     double best = 0.0;
     bool found = false;
     for (int ks = 1; ks <= 8; ks *= 2) {
-        const int target = (q.nb + ks - 1) / ks;
-        const int qmin = (target * bb + 1007) / 1008;
-        for (int nq = qmin; nq <= qmin + 4; ++nq) {
-            const int kc = ((target + nq - 1) / nq + align - 1) / align * align;
-            int pitch = (kc * bb + 15) / 16 * 16;
-            if (((pitch / 4) & 7) != 4) pitch += 16;
-            if (pitch > 1024) continue;
-            const int nbs = nq * kc;
-            if (ks > 1 && (long)nbs * (ks - 1) >= q.nb) continue;  // a slice without blocks
-            const size_t fixed = band_layout(0, pitch, nbs, q.M, kBandW).total;
-            if (fixed + 3 * 32 * (size_t)pitch > kBandSmemMax) continue;
-            int S = (int)((kBandSmemMax - fixed) / (32 * (size_t)pitch));
-            if (S > 8) S = 8;
-            const size_t smem = band_layout(S, pitch, nbs, q.M, kBandW).total;
-            int cap = band_capacity(q.qt, kBandW, q.M, smem);
-            if (cap <= 0) cap = num_sms;
-            long grid = cap < (long)tiles * ks ? cap : (long)tiles * ks;
-            grid -= grid % ks;
-            if (grid < ks) continue;
-            const long per_slice = grid / ks;
-            const long rounds = (tiles + per_slice - 1) / per_slice;
-            const int nch = ks == 1 ? (q.nb + kc - 1) / kc : nq;  // chunks of the longest slice
-            const double boxes = (double)rounds * nch;
-            const double bytes = boxes * 32.0 * pitch;
-            // shallow rings lose bandwidth (measured: 3 stages ~13% below 6)
-            const double depth = S >= 5 ? 1.0 : (S == 4 ? 1.05 : 1.13);
-            const double cost =
-                (bytes > boxes * kBandBoxFloor ? bytes : boxes * kBandBoxFloor) * depth * (ks > 1 ? 1.02 : 1.0);
-            if (!found || cost < best) {
-                found = true;
-                best = cost;
-                q.ks = ks;
-                q.nbu = nbs;
-                q.kc = kc;
-                q.pitch = pitch;
-                q.sw = S;
-                q.smem = smem;
-                q.grid = (int)grid;
-            }
+        const int nq = ((q.nb + ks - 1) / ks + kc - 1) / kc;  // chunks per slice
+        const int nbs = nq * kc;
+        if (ks > 1 && (long)nbs * (ks - 1) >= q.nb) continue;  // a slice without blocks
+        const size_t fixed = band_layout(0, pitch, nbs, mt, kBandWarps).total;
+        if (fixed + 3 * 32 * (size_t)pitch > kBandSmemMax) continue;
+        int S = (int)((kBandSmemMax - fixed) / (32 * (size_t)pitch));
+        if (S > 8) S = 8;
+        const size_t smem = band_layout(S, pitch, nbs, mt, kBandWarps).total;
+        int cap = band_capacity(q.qt, q.M, smem);
+        if (cap <= 0) cap = num_sms;
+        long grid = cap < (long)tiles * ks ? cap : (long)tiles * ks;
+        grid -= grid % ks;
+        if (grid < ks) continue;
+        const long per_slice = grid / ks;
+        const long rounds = (tiles + per_slice - 1) / per_slice;
+        // shallow rings lose bandwidth (measured: 3 stages ~13% below 6)
+        const double depth = S >= 5 ? 1.0 : (S == 4 ? 1.05 : 1.13);
+        const double cost = (double)rounds * nq * 32.0 * pitch * depth * (ks > 1 ? 1.02 : 1.0);
+        if (!found || cost < best) {
+            found = true;
+            best = cost;
+            q.ks = ks;
+            q.nbu = nbs;
+            q.sw = S;
+            q.smem = smem;
+            q.grid = (int)grid;
         }
     }
     if (!found) return false;
     q.kind = kGemvBand;
-    q.tw = kBandW;
+    q.kc = kc;
+    q.pitch = pitch;
+    q.tw = kBandWarps;
     q.cluster = 1;
     q.loader = kLoaderTma2d;
     q.units = 0;

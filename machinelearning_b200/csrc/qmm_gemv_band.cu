@@ -60,12 +60,46 @@ struct BandThreads {
     static constexpr int kTotal = 32 * (W + 2);  // producer, consumers, reducer
 };
 
-template <int QT, int W, bool PACK>
-__global__ void __launch_bounds__(BandThreads<W>::kTotal, 1) gemv_band_kernel(const __grid_constant__ BArgs a) {
+// Blocks JB..BPW-1 of a consumer warp's share of a chunk (compile-time
+// offsets: every shared load is [register + immediate]).
+struct BandLane {
+    uint32_t rg, rg8, rg16, rg24;      // rows g, g+8, g+16, g+24 at the warp's first block
+    uint32_t rgt, rg8t, rg16t, rg24t;  // the same plus the lane's payload word
+    uint32_t xa;                       // the lane's activation record (column g) at that block
+    uint32_t sa;                       // the lane's token terms at that block
+};
+template <int QT, int MT, int BPW, int JB>
+__device__ __forceinline__ void band_blocks(const BandLane& l, bool xvalid, float (&acc)[2][2]) {
+    if constexpr (JB < BPW) {
+        constexpr int BB = block_bytes(QT);
+        constexpr int NP = (MT + 1) / 2;
+        constexpr int OFF = JB * BB, XO = JB * MT * 64, SO = JB * NP * 32;
+        // chunks start 16-byte aligned and an even number of blocks into the
+        // row: payloads of odd blocks are 4-byte aligned (Q8_0, Q4_0), Q4_1
+        // payloads always are
+        constexpr bool AL = QT == kQ4_1 || (JB & 1);
+        uint4 xb = make_uint4(0, 0, 0, 0);
+        lds128_at_if<XO>(xb, l.xa, xvalid);
+        const float cs = __uint_as_float(lds32_at<SO>(l.sa));
+        const float ss = __uint_as_float(lds32_at<SO + 16>(l.sa));
+        const float sx = QT == kQ4_1 ? __uint_as_float(lds32_at<SO + 24>(l.sa)) : 0.0f;
+        consume_group_packed_sa<QT, AL, OFF>(l.rg, l.rg8, l.rgt, l.rg8t, xb, cs, ss, sx, acc[0]);
+        consume_group_packed_sa<QT, AL, OFF>(l.rg16, l.rg24, l.rg16t, l.rg24t, xb, cs, ss, sx, acc[1]);
+        band_blocks<QT, MT, BPW, JB + 1>(l, xvalid, acc);
+    }
+}
+
+template <int QT, int MT>
+__global__ void __launch_bounds__(BandThreads<kBandWarps>::kTotal, 1)
+    gemv_band_kernel(const __grid_constant__ BArgs a) {
+    constexpr int W = kBandWarps;
+    constexpr int BPW = band_bpw(QT);  // blocks per consumer warp per chunk (even)
+    constexpr int KC = W * BPW;         // blocks per chunk
+    constexpr int NP = (MT + 1) / 2;    // token pairs of the side records
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int BB = block_bytes(QT);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const BandLayout L = band_layout(a.S, a.pitch, a.nbs, a.M, W);
+    const BandLayout L = band_layout(a.S, a.pitch, a.nbs, MT, W);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
     uint64_t* full = bars;
     uint64_t* empty = bars + a.S;
@@ -77,9 +111,8 @@ __global__ void __launch_bounds__(BandThreads<W>::kTotal, 1) gemv_band_kernel(co
     const int tfirst = (int)blockIdx.x / ks;
     const int kb0 = slice * a.nbs;                          // this CTA's first block
     const int nbc = max(0, min(a.nb - kb0, a.nbs));         // its blocks
-    const int nch = (nbc + a.kc - 1) / a.kc;                // chunks per tile
+    const int nch = (nbc + KC - 1) / KC;                    // chunks per tile
     const int ntile = a.tiles > tfirst ? (a.tiles - tfirst + tstep - 1) / tstep : 0;  // its tiles
-    const int npair = (a.M + 1) / 2;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < a.S; ++i) {
@@ -107,7 +140,7 @@ __global__ void __launch_bounds__(BandThreads<W>::kTotal, 1) gemv_band_kernel(co
                 const int s = i % a.S;
                 if (i >= a.S && !mbar_wait_bounded(&empty[s], ((i / a.S) - 1) & 1, a.err)) break;
                 const int tile = tfirst + (i / nch) * tstep;
-                const int cb0 = kb0 + (i % nch) * a.kc;
+                const int cb0 = kb0 + (i % nch) * KC;
                 // rows past N and columns past the row end are zero-filled and counted
                 mbar_arrive_expect_tx(&full[s], stage_bytes);
                 tma_load_2d(smem + L.ring + (uint32_t)s * stage_bytes, &a.tmap, cb0 * BB / 4, tile * 32, &full[s]);
@@ -118,108 +151,64 @@ __global__ void __launch_bounds__(BandThreads<W>::kTotal, 1) gemv_band_kernel(co
     } else if (warp <= W) {
         // ---------------- consumers ---------------------------------------------------------
         const int cw = warp - 1;
+        const int ctid = threadIdx.x - 32;
+        // activation records: zero first (tokens M..MT-1 and the blocks of a
+        // chunk past the slice contribute exactly zero), then fill
+        {
+            uint4* z = reinterpret_cast<uint4*>(smem + L.xf);
+            const int nz = (int)((L.part - L.xf) / 16);
+            for (int i = ctid; i < nz; i += BandThreads<W>::kConsumers) z[i] = make_uint4(0, 0, 0, 0);
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(BandThreads<W>::kConsumers) : "memory");
         pdl_wait();  // x comes from the preceding work in the stream
-        const uint32_t lo_plane = (uint32_t)nbc * (uint32_t)a.M * 64u;
-        prep_x_smem<QT>(a.x, a.M, a.K, kb0, nbc, smem + L.xf, lo_plane, reinterpret_cast<uint32_t*>(smem + L.side),
-                        npair, threadIdx.x - 32, BandThreads<W>::kConsumers);
+        const uint32_t lo_plane = (uint32_t)a.nbs * MT * 64u;
+        prep_x_smem<QT>(a.x, a.M, a.K, kb0, nbc, smem + L.xf, lo_plane, reinterpret_cast<uint32_t*>(smem + L.side), NP,
+                        ctid, BandThreads<W>::kConsumers, MT);
         asm volatile("bar.sync 1, %0;" ::"r"(BandThreads<W>::kConsumers) : "memory");
         const int g = lane >> 2, t = lane & 3;
-        // the side record a lane reads: its token (PACK) or token pair; lanes
-        // past M read the last valid one (their tokens are not stored)
-        const int tp = PACK ? min(t, a.M - 1) : 2 * min(t, npair - 1);
-        const uint8_t* xfb = smem + L.xf;
-        const uint4* sd = reinterpret_cast<const uint4*>(smem + L.side);
+        // lane (g, t) supplies MMA column g (token g / 2, hi or lo half) and
+        // receives token t (lanes past M read token M - 1's terms: not stored)
+        const int tp = min(t, a.M - 1);
+        const bool xvalid = g < 2 * a.M;
+        const uint32_t xl = smem_u32(smem + L.xf) + ((uint32_t)((cw * BPW) * MT + (g >> 1)) * 4 + t) * 16 +
+                            ((g & 1) ? lo_plane : 0u);
+        const uint32_t sl = smem_u32(smem + L.side) + (((cw * BPW) * NP + (tp >> 1)) * 8 + (tp & 1)) * 4;
+        const uint32_t ring0 = smem_u32(smem + L.ring) + (uint32_t)(g * a.pitch) + (uint32_t)(cw * BPW * BB);
         float* part = reinterpret_cast<float*>(smem + L.part);
         bool ok = true;
         int i = 0;  // chunks consumed
-        const uint32_t* sw = reinterpret_cast<const uint32_t*>(smem + L.side);
         for (int j = 0; j < ntile && ok; ++j) {
-            float acc[2][1][4];
-#pragma unroll
-            for (int r = 0; r < 2; ++r) acc[r][0][0] = acc[r][0][1] = acc[r][0][2] = acc[r][0][3] = 0.0f;
+            float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // [row group][rows g, g + 8] for token t
             for (int c = 0; c < nch; ++c, ++i) {
                 const int s = i % a.S;
                 if (!mbar_wait_bounded(&full[s], (i / a.S) & 1, a.err)) {
                     ok = false;
                     break;
                 }
-                const int cbl = c * a.kc;  // chunk start, slice-relative
-                const int cbn = min(a.kc, nbc - cbl);
-                const int b_begin = cbl + cbn * cw / W, b_end = cbl + cbn * (cw + 1) / W;
-                const uint8_t* sbase = smem + L.ring + (uint32_t)s * 32u * (uint32_t)a.pitch - (uint32_t)cbl * BB;
-                const uint8_t* r0 = sbase + g * a.pitch;
-                const uint8_t* r8 = r0 + 8 * a.pitch;
-                const uint8_t* r16 = r0 + 16 * a.pitch;
-                const uint8_t* r24 = r0 + 24 * a.pitch;
-                auto block = [&](int b, auto aligned) {
-                    constexpr bool AL = decltype(aligned)::value;
-                    const uint32_t o = (uint32_t)b * BB;
-                    if constexpr (PACK) {
-                        // column g: token g / 2, hi (even g) or lo (odd g); lanes
-                        // t < M receive token t
-                        uint4 xb = make_uint4(0, 0, 0, 0);
-                        if (g < 2 * a.M)
-                            xb = *reinterpret_cast<const uint4*>(xfb + ((uint32_t)(b * a.M + (g >> 1)) * 4 + t) * 16 +
-                                                                 ((g & 1) ? lo_plane : 0u));
-                        const uint32_t* rec = sw + (b * npair + (tp >> 1)) * 8 + (tp & 1);
-                        const float cs = __uint_as_float(rec[0]), sc = __uint_as_float(rec[4]);
-                        const float sx = QT == kQ4_1 ? __uint_as_float(rec[6]) : 0.0f;
-                        float a0[2] = {acc[0][0][0], acc[0][0][2]}, a1[2] = {acc[1][0][0], acc[1][0][2]};
-                        consume_group_packed<QT, AL>(r0 + o, r8 + o, t, xb, cs, sc, sx, a0);
-                        consume_group_packed<QT, AL>(r16 + o, r24 + o, t, xb, cs, sc, sx, a1);
-                        acc[0][0][0] = a0[0];
-                        acc[0][0][2] = a0[1];
-                        acc[1][0][0] = a1[0];
-                        acc[1][0][2] = a1[1];
-                    } else {
-                        XFrag xr[1];
-                        if (g < a.M) {
-                            const uint8_t* p = xfb + ((uint32_t)(b * a.M + g) * 4 + t) * 16;
-                            xr[0].hi = *reinterpret_cast<const uint4*>(p);
-                            xr[0].lo = *reinterpret_cast<const uint4*>(p + lo_plane);
-                        } else {
-                            xr[0].hi = make_uint4(0, 0, 0, 0);
-                            xr[0].lo = make_uint4(0, 0, 0, 0);
-                        }
-                        xr[0].c4 = sd[(b * npair + (tp >> 1)) * 2];
-                        xr[0].s4 = sd[(b * npair + (tp >> 1)) * 2 + 1];
-                        consume_group<QT, 1, false, AL, true>(r0 + o, r8 + o, t, xr, acc[0]);
-                        consume_group<QT, 1, false, AL, true>(r16 + o, r24 + o, t, xr, acc[1]);
-                    }
-                };
-                // chunks start 16-byte aligned in shared memory and a multiple
-                // of 8 (Q4_1: 4) blocks into the row, so payload alignment
-                // follows block parity as in a dense TMA tile
-                using EvenAl = std::integral_constant<bool, QT == kQ4_1>;
-                using OddAl = std::true_type;
-                int b = b_begin;
-                if (b < b_end && (b & 1)) block(b++, OddAl{});
-                for (; b + 1 < b_end; b += 2) {
-                    block(b, EvenAl{});
-                    block(b + 1, OddAl{});
-                }
-                if (b < b_end) block(b, EvenAl{});
+                BandLane l;
+                l.rg = ring0 + (uint32_t)s * 32u * (uint32_t)a.pitch;
+                l.rg8 = l.rg + 8u * (uint32_t)a.pitch;
+                l.rg16 = l.rg + 16u * (uint32_t)a.pitch;
+                l.rg24 = l.rg + 24u * (uint32_t)a.pitch;
+                l.rgt = l.rg + 4u * t;
+                l.rg8t = l.rg8 + 4u * t;
+                l.rg16t = l.rg16 + 4u * t;
+                l.rg24t = l.rg24 + 4u * t;
+                l.xa = xl + (uint32_t)(c * KC) * MT * 64u;
+                l.sa = sl + (uint32_t)(c * KC) * NP * 32u;
+                band_blocks<QT, MT, BPW, 0>(l, xvalid, acc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (!ok) break;
             const int slot = j & 1;
             if (j >= 2 && !mbar_wait_bounded(&rempty[slot], ((j >> 1) - 1) & 1, a.err)) break;
+            // lane (g, t): token t of rows g, g + 8, g + 16, g + 24
             float* pw = part + ((size_t)slot * W + cw) * 32 * 8;
-            if constexpr (PACK) {
-                // lane (g, t): token t of rows g, g + 8, g + 16, g + 24
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    pw[(16 * r + g) * 8 + t] = acc[r][0][0];
-                    pw[(16 * r + g + 8) * 8 + t] = acc[r][0][2];
-                }
-            } else {
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    float* p0 = pw + (16 * r + g) * 8 + 2 * t;
-                    *reinterpret_cast<float2*>(p0) = make_float2(acc[r][0][0], acc[r][0][1]);
-                    *reinterpret_cast<float2*>(p0 + 64) = make_float2(acc[r][0][2], acc[r][0][3]);  // row + 8
-                }
+            for (int r = 0; r < 2; ++r) {
+                pw[(16 * r + g) * 8 + t] = acc[r][0];
+                pw[(16 * r + g + 8) * 8 + t] = acc[r][1];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&rfull[slot]);
@@ -292,25 +281,27 @@ __global__ void __launch_bounds__(BandThreads<W>::kTotal, 1) gemv_band_kernel(co
     }
 }
 
-template <int QT, bool PACK>
-const void* band_kernel_w(int W) {
-    return W == 16 ? (const void*)gemv_band_kernel<QT, 16, PACK> : (const void*)gemv_band_kernel<QT, 8, PACK>;
+// One token (decode at batch 1); the kernel is written for up to 4 (MT), the
+// planner routes M = 1 only (measured: no gain over the streaming kernel yet
+// for 2 to 4 tokens).
+template <int QT>
+const void* band_kernel_m(int M) {
+    (void)M;
+    return (const void*)gemv_band_kernel<QT, 1>;
 }
 
-// PACK (hi/lo halves in separate MMA columns) for up to 4 tokens
-const void* band_kernel_for(int qt, int W, int M) {
-    const bool pack = M <= 4;
-    if (qt == kQ8_0) return pack ? band_kernel_w<kQ8_0, true>(W) : band_kernel_w<kQ8_0, false>(W);
-    if (qt == kQ4_0) return pack ? band_kernel_w<kQ4_0, true>(W) : band_kernel_w<kQ4_0, false>(W);
-    return pack ? band_kernel_w<kQ4_1, true>(W) : band_kernel_w<kQ4_1, false>(W);
+const void* band_kernel_for(int qt, int M) {
+    if (qt == kQ8_0) return band_kernel_m<kQ8_0>(M);
+    if (qt == kQ4_0) return band_kernel_m<kQ4_0>(M);
+    return band_kernel_m<kQ4_1>(M);
 }
 
 }  // namespace
 
-int band_threads(int W) { return 32 * (W + 2); }
+int band_threads() { return BandThreads<kBandWarps>::kTotal; }
 
-int band_capacity(int qt, int W, int M, size_t smem) {
-    const void* fn = band_kernel_for(qt, W, M);
+int band_capacity(int qt, int M, size_t smem) {
+    const void* fn = band_kernel_for(qt, M);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
     struct Entry {
@@ -330,7 +321,7 @@ int band_capacity(int qt, int W, int M, size_t smem) {
     int cap = 0;
     if (ensure_dynamic_smem(fn, smem) == cudaSuccess) {
         int per_sm = 0, sms = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, band_threads(W), smem) == cudaSuccess &&
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, band_threads(), smem) == cudaSuccess &&
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
             cap = per_sm * sms;
     }
@@ -342,7 +333,7 @@ int band_capacity(int qt, int W, int M, size_t smem) {
 cudaError_t launch_gemv_band(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y,
                              const GemvWorkspace& ws, int* err, cudaStream_t st, bool no_host_alloc,
                              const GatedOut& g) {
-    const void* fn = band_kernel_for(p.qt, p.tw, p.M);
+    const void* fn = band_kernel_for(p.qt, p.M);
     cudaError_t e = no_host_alloc ? set_max_dynamic_smem(fn) : ensure_dynamic_smem(fn, p.smem);
     if (e != cudaSuccess) return e;
     const int tiles = (p.N + kRows - 1) / kRows;
@@ -373,7 +364,7 @@ cudaError_t launch_gemv_band(const GemvPlan& p, const CUtensorMap& tmap, const f
     a.gout = g.out;
     a.ghidden = g.hidden;
     void* args[] = {(void*)&a};
-    return launch_pdl_kernel(fn, dim3(p.grid), dim3(band_threads(p.tw)), p.smem, st, args);
+    return launch_pdl_kernel(fn, dim3(p.grid), dim3(band_threads()), p.smem, st, args);
 }
 
 }  // namespace qmm

@@ -243,4 +243,87 @@ __device__ __forceinline__ void consume_group_packed(const uint8_t* r0, const ui
     }
 }
 
+// ---- shared loads at a 32-bit address plus a compile-time offset ---------------------
+// Volatile (kept in order with the mbarrier waits, which are volatile too) but
+// without a memory clobber, so independent arithmetic can move around them.
+template <int OFF>
+__device__ __forceinline__ uint32_t lds16_at(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1+%2];" : "=h"(v) : "r"(a), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint32_t lds32_at(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
+    return v;
+}
+// 4 bytes at a + OFF: AL = 4-byte aligned, else 2-byte aligned (two halves).
+template <int OFF, bool AL>
+__device__ __forceinline__ uint32_t ldsw_at(uint32_t a) {
+    if constexpr (AL) return lds32_at<OFF>(a);
+    return __byte_perm(lds16_at<OFF>(a), lds16_at<OFF + 2>(a), 0x5410);
+}
+// 16 bytes at a + OFF into x when p (x unchanged otherwise).
+template <int OFF>
+__device__ __forceinline__ void lds128_at_if(uint4& x, uint32_t a, bool p) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %4, 0;\n\t"
+        "@q ld.shared.v4.u32 {%0, %1, %2, %3}, [%5+%6];\n\t}"
+        : "+r"(x.x), "+r"(x.y), "+r"(x.z), "+r"(x.w)
+        : "r"((uint32_t)p), "r"(a), "n"(OFF));
+}
+
+// consume_group_packed on 32-bit shared addresses: rg / rg8 are the stage
+// addresses of rows g / g + 8 at the chunk's first block, OFF the block's byte
+// offset in the row, rgt / rg8t the same plus the lane's payload word (4t).
+template <int QT, bool AL, int OFF>
+__device__ __forceinline__ void consume_group_packed_sa(uint32_t rg, uint32_t rg8, uint32_t rgt, uint32_t rg8t,
+                                                        uint4 xb, float c, float s, float sx, float (&acc)[2]) {
+    const float d0 = f16_bits_to_f32((uint16_t)lds16_at<OFF>(rg));
+    const float d1 = f16_bits_to_f32((uint16_t)lds16_at<OFF>(rg8));
+    constexpr int NOFF = (QT == kQ4_1) ? 4 : 2;
+    uint32_t A0[4], A1[4];
+    if constexpr (QT == kQ8_0) {
+        const uint32_t u00 = ldsw_at<OFF + NOFF, AL>(rgt) ^ 0x80808080u;
+        const uint32_t u01 = ldsw_at<OFF + NOFF + 16, AL>(rgt) ^ 0x80808080u;
+        const uint32_t u10 = ldsw_at<OFF + NOFF, AL>(rg8t) ^ 0x80808080u;
+        const uint32_t u11 = ldsw_at<OFF + NOFF + 16, AL>(rg8t) ^ 0x80808080u;
+        A0[0] = __byte_perm(u00, 0x64646464u, 0x4140);
+        A0[1] = __byte_perm(u10, 0x64646464u, 0x4140);
+        A0[2] = __byte_perm(u00, 0x64646464u, 0x4342);
+        A0[3] = __byte_perm(u10, 0x64646464u, 0x4342);
+        A1[0] = __byte_perm(u01, 0x64646464u, 0x4140);
+        A1[1] = __byte_perm(u11, 0x64646464u, 0x4140);
+        A1[2] = __byte_perm(u01, 0x64646464u, 0x4342);
+        A1[3] = __byte_perm(u11, 0x64646464u, 0x4342);
+    } else {
+        const uint32_t w0 = ldsw_at<OFF + NOFF, AL>(rgt);
+        const uint32_t w1 = ldsw_at<OFF + NOFF, AL>(rg8t);
+        const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
+        A0[0] = lop3_and_or(w0, 0x000F000Fu, 0x64006400u);
+        A0[1] = lop3_and_or(w1, 0x000F000Fu, 0x64006400u);
+        A0[2] = lop3_and_or(w0s, 0x000F000Fu, 0x64006400u);
+        A0[3] = lop3_and_or(w1s, 0x000F000Fu, 0x64006400u);
+        A1[0] = lop3_and_or(w0, 0x00F000F0u, 0x64006400u);
+        A1[1] = lop3_and_or(w1, 0x00F000F0u, 0x64006400u);
+        A1[2] = lop3_and_or(w0s, 0x00F000F0u, 0x64006400u);
+        A1[3] = lop3_and_or(w1s, 0x00F000F0u, 0x64006400u);
+    }
+    const float c0[4] = {c, 0.0f, c, 0.0f};
+    float e[4], h[4];
+    mma_f16_c(e, A0, xb.x, xb.y, c0);
+    mma_f16_c(h, A1, xb.z, xb.w, e);
+    const float v0 = h[0] + h[1], v1 = h[2] + h[3];  // hi + lo, rows g and g + 8
+    if constexpr (QT == kQ4_1) {
+        const float m0 = f16_bits_to_f32((uint16_t)lds16_at<OFF + 2>(rg));
+        const float m1 = f16_bits_to_f32((uint16_t)lds16_at<OFF + 2>(rg8));
+        acc[0] = fmaf(s, fmaf(d0, v0, m0 * sx), acc[0]);
+        acc[1] = fmaf(s, fmaf(d1, v1, m1 * sx), acc[1]);
+    } else {
+        acc[0] = fmaf(d0 * s, v0, acc[0]);
+        acc[1] = fmaf(d1 * s, v1, acc[1]);
+    }
+}
+
 }  // namespace qmm

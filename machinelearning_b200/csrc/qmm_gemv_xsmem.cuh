@@ -63,11 +63,13 @@ __device__ __forceinline__ int frexp_exponent(float a) {
 // as written by xprep_f32_kernel: xf [nbc][M][4] x 16 B (hi plane; the lo
 // plane lo_plane bytes further), side [nbc][npair][8 words] with npair token
 // pairs per block (npair >= ceil(M / 2)); tokens M..2*npair-1 get neutral side
-// records. The caller synchronises before reading them.
+// records. mstride >= M: tokens per block in the xf planes (records of tokens
+// M..mstride-1 are not written). The caller synchronises before reading them.
 template <int QT>
 __device__ __forceinline__ void prep_x_smem(const float* __restrict__ x, int M, int K, int kb0, int nbc,
                                             uint8_t* xf, uint32_t lo_plane, uint32_t* side, int npair, int tid,
-                                            int nthreads) {
+                                            int nthreads, int mstride = 0) {
+    if (mstride < M) mstride = M;
     const int warp = tid >> 5, lane = tid & 31;
     {
         const int npt = 2 * npair - M;  // padding tokens per block: neutral records
@@ -151,7 +153,7 @@ __device__ __forceinline__ void prep_x_smem(const float* __restrict__ x, int M, 
             if (live) {
                 // thread t's 16-byte record holds elements 4t..4t+3 then
                 // 16+4t..16+4t+3, in the hi plane and in the lo plane
-                uint8_t* rec = xf + ((uint32_t)(b * M + m) * 4 + (gl & 3)) * 16 + (upper ? 8 : 0);
+                uint8_t* rec = xf + ((uint32_t)(b * mstride + m) * 4 + (gl & 3)) * 16 + (upper ? 8 : 0);
                 *reinterpret_cast<uint2*>(rec) = make_uint2(h2_bits(h01), h2_bits(h23));
                 *reinterpret_cast<uint2*>(rec + lo_plane) = make_uint2(h2_bits(l01), h2_bits(l23));
                 if (gl == 0) {

@@ -110,9 +110,19 @@ __host__ __device__ inline ResidentLayout resident_layout(int tw, int gpc, int p
     return L;
 }
 
+// Band kernel geometry: consumer warps per CTA and blocks per warp per chunk
+// (even: payload alignment then follows the block index); a chunk (one TMA
+// box of 32 rows) is kBandWarps * band_bpw(qt) blocks: 48 Q4_0 / Q4_1 (880 /
+// 976-byte rows), 24 Q8_0 (816-byte rows).
+constexpr int kBandWarps = 12;
+__host__ __device__ constexpr int band_bpw(int qt) { return qt == 8 ? 2 : 4; }
+// Token capacity of the band kernel variant for M tokens (M <= 4).
+__host__ __device__ constexpr int band_mt(int M) { return M <= 1 ? 1 : (M == 2 ? 2 : 4); }
+
 // Shared-memory layout of the band kernel (byte offsets), host and device:
 // S ring stages of 32 rows x pitch, activations of nbs blocks x M tokens
-// (side records for ceil(M / 2) token pairs), W consumer warps.
+// (M: the variant's token capacity; side records for ceil(M / 2) token
+// pairs), W consumer warps.
 struct BandLayout {
     uint32_t ring, xf, side, part, bar, total;
 };
@@ -155,14 +165,14 @@ cudaError_t launch_gemv(const GemvPlan& p, const uint8_t* w, const float* x, flo
                         int* err, cudaStream_t st, bool no_host_alloc = false, const GatedOut& g = GatedOut());
 
 // The band kernel (launch_gemv dispatches kGemvBand plans to it; tmap: the
-// weights with a [pitch / 4, 32] box), threads per CTA for W consumer warps,
-// and how many of its CTAs with `smem` bytes fit on the current device at
-// once (0: unknown).
+// weights with a [pitch / 4, 32] box), threads per CTA, and how many of its
+// CTAs (the variant for M tokens) with `smem` bytes fit on the current device
+// at once (0: unknown).
 cudaError_t launch_gemv_band(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y,
                              const GemvWorkspace& ws, int* err, cudaStream_t st, bool no_host_alloc,
                              const GatedOut& g);
-int band_threads(int W);
-int band_capacity(int qt, int W, int M, size_t smem);
+int band_threads();
+int band_capacity(int qt, int M, size_t smem);
 
 // The resident kernel (launch_gemv dispatches to it for kGemvResident plans).
 cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, const float* x, float* y, int* err,

@@ -253,16 +253,19 @@ def test_resident_kernel_variants(oracle, torch_cuda, qlib, case):
     check(oracle, torch_cuda, qlib, dt, 1, x, w, m, k, n)
 
 
-# Band kernel (M <= 8, f32 activations, 16-byte row pitch, weights above what
-# the resident kernel holds on chip: > ~30 MB): K slices over clusters, ragged
-# last tiles, a shorter last slice, every block type. One launch per call.
+# Band kernel (M = 1, f32 activations, 16-byte row pitch, weights above what
+# the resident kernel holds on chip: > ~30 MB): K slices, ragged last tiles,
+# partial last chunks, every block type. One kernel per call (K splits add a
+# memset of the tickets).
 BAND = [
     (Q4_0, 1, 16384, 4100),  # ragged last tile (4 rows)
     (Q8_0, 1, 8192, 5000),
     (Q4_1, 1, 12288, 7000),  # 20-byte blocks
     (Q8_0, 1, 14336, 4096),
-    (Q4_0, 1, 8448, 9000),   # 264 blocks: the last K slice is shorter
+    (Q4_0, 1, 8448, 9000),   # 264 blocks: partial last chunk
     (Q4_0, 1, 8192, 28672),  # Llama-70B gate
+    (Q4_1, 1, 28672, 2048),  # long K: split into slices
+    (Q8_0, 1, 28672, 1120),
 ]
 
 

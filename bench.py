@@ -118,15 +118,17 @@ def load_peaks(tensor=False):
 
 
 def profiled_traffic(workload):
-    """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary
-    (profiles/gemv_<workload>.md, line 'traffic_bytes_per_launch: <n>')."""
-    path = os.path.join(ROOT, "profiles", f"gemv_{workload}.md")
-    try:
-        for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1])
-    except OSError:
-        pass
+    """Per-launch DRAM bytes of the workload's dominant kernel from the committed
+    ncu summary (profiles/<kernel>_<workload>.md, line
+    'traffic_bytes_per_launch: <n>')."""
+    import glob
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", f"*_{workload}.md"))):
+        try:
+            for line in open(path):
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1])
+        except OSError:
+            pass
     return None
 
 

@@ -48,20 +48,25 @@ namespace qmm {
 namespace {
 
 constexpr int BM = 128;            // tokens per accumulator (MMA M, TMEM lanes)
-constexpr int BN = 128;            // weight rows per tile (MMA N, TMEM columns)
+constexpr int BN = 128;            // weight rows per tile by default (MMA N, TMEM columns); 160 also built
 constexpr int BK = 64;             // f16 elements per K step: one 128-byte swizzle row
 constexpr int kStepsPerChunk = 4;  // a raw chunk is 8 blocks = 256 elements
 constexpr int SR = 2;              // raw chunk stages
-constexpr int kDqWarps = 8;        // dequantising (then epilogue) warps
-constexpr int kDqThreads = 32 * kDqWarps;
-constexpr int kGemmThreads = 64 + kDqThreads + 32;  // + the raw-chunk producer warp
-constexpr uint32_t kTileBytes = BM * BK * 2;  // 16 KB: 128 rows x 128 bytes
+// Per weight-tile width W (128 or 160 rows): W / 16 dequantising (then
+// epilogue) warps, one (row, block) per thread per K step; 2 + W / 16 + 1 warps
+// in all (x16 producer, MMA issuer, dequantisers, raw-chunk producer).
+__host__ __device__ constexpr int dq_warps(int W) { return W / 16; }
+__host__ __device__ constexpr int dq_threads(int W) { return 2 * W; }
+__host__ __device__ constexpr int gemm_threads(int W) { return 64 + dq_threads(W) + 32; }
+constexpr uint32_t kTileBytes = BM * BK * 2;  // 16 KB: 128 rows x 128 bytes (x16 tile)
 
 // Operand rings: the x16 (A) ring is the deeper one -- its TMA loads take
 // 1.5-2 us to land under load, and a stage is refilled only once the MMAs
 // that read it have completed -- while dequantised weight tiles (B) are ready
 // ~0.3 us after their raw chunk is. Sized to fill 227 KB with the raw ring.
-__host__ __device__ constexpr int a_stages(int qt, int T) { return T == 1 ? 6 : (qt == kQ8_0 ? 3 : 4); }
+__host__ __device__ constexpr int a_stages(int qt, int T, int W = BN) {
+    return T == 1 ? 6 : (W > BN ? 3 : (qt == kQ8_0 ? 3 : 4));
+}
 __host__ __device__ constexpr int b_stages(int, int) { return 3; }
 
 // Raw chunk row pitch in shared memory (= the TMA box's inner extent): 8
@@ -83,11 +88,14 @@ struct GArgs {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-size_t gemm_smem_bytes(int qt, int T) {
-    const int SA = a_stages(qt, T), SB = b_stages(qt, T);
-    return 1024 + (size_t)(SA * T + SB) * kTileBytes + (size_t)SR * BN * raw_pitch(qt) + (2 * SA + 2 * SB + 2 * SR + 1) * 8 +
-           16;
+__host__ __device__ constexpr size_t gemm_smem_bytes(int qt, int T, int W) {
+    return 1024 + (size_t)a_stages(qt, T, W) * T * kTileBytes + (size_t)b_stages(qt, T) * W * BK * 2 +
+           (size_t)SR * W * raw_pitch(qt) + (2 * a_stages(qt, T, W) + 2 * b_stages(qt, T) + 2 * SR + 1) * 8 + 16;
 }
+static_assert(gemm_smem_bytes(kQ4_0, 2, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 2, 160) <= 232448 &&
+                  gemm_smem_bytes(kQ4_0, 1, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 1, 160) <= 232448 &&
+                  gemm_smem_bytes(kQ8_0, 2, BN) <= 232448 && gemm_smem_bytes(kQ4_1, 2, BN) <= 232448,
+              "a GEMM variant exceeds 227 KB of shared memory");
 
 // ---- tcgen05 / TMEM --------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
@@ -146,7 +154,9 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 // Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both
 // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+__host__ __device__ constexpr uint32_t gemm_idesc(int W) {
+    return (1u << 4) | ((uint32_t)(W >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
 
 // ---- dequantisation to f16 pairs --------------------------------------------------------
 __device__ __forceinline__ __half2 as_h2(uint32_t v) {
@@ -315,16 +325,19 @@ __global__ void gemm_xprep_kernel(const float* __restrict__ x, int M, int K, __h
     if (threadIdx.x == 0) xs[m] = __int_as_float((e + 127) << 23);
 }
 
-template <int QT, int T>
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GArgs a) {
-    constexpr int SA = a_stages(QT, T), SB = b_stages(QT, T);
+template <int QT, int T, int W>
+__global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_constant__ GArgs a) {
+    constexpr int SA = a_stages(QT, T, W), SB = b_stages(QT, T);
+    constexpr int kDqWarps = dq_warps(W), kDqThreads = dq_threads(W);
+    constexpr uint32_t kBTile = (uint32_t)W * BK * 2;  // dequantised weight tile bytes
+    constexpr uint32_t kTmemCols = T * W <= 128 ? 128 : (T * W <= 256 ? 256 : 512);
     constexpr int PITCH = raw_pitch(QT);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                        // [SA][T] x16 tiles
     uint8_t* sB = smem + SA * T * kTileBytes;  // [SB] weight tiles
-    uint8_t* sR = sB + SB * kTileBytes;        // [SR] raw chunks
-    uint64_t* full_a = reinterpret_cast<uint64_t*>(sR + SR * BN * PITCH);
+    uint8_t* sR = sB + SB * kBTile;            // [SR] raw chunks
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(sR + SR * W * PITCH);
     uint64_t* empty_a = full_a + SA;
     uint64_t* full_b = empty_a + SA;
     uint64_t* empty_b = full_b + SB;
@@ -334,7 +347,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * (T * BM);
+    const int n0 = blockIdx.x * W, m0 = blockIdx.y * (T * BM);
     const int nchunks = (a.ksteps + kStepsPerChunk - 1) / kStepsPerChunk;
     // Every CTA starts its K loop at a different raw chunk: CTAs that share a
     // token tile then fetch different x16 tiles at any moment instead of all
@@ -362,7 +375,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         prefetch_tmap(&a.tmap_w);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, T * BN);
+        tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -398,7 +411,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             for (int i = (a_issued > SA ? a_issued - SA : 0); i < a_issued; ++i)
                 mbar_wait_bounded(&full_a[i % SA], (i / SA) & 1, nullptr);
         }
-    } else if (warp == kGemmThreads / 32 - 1) {
+    } else if (warp == gemm_threads(W) / 32 - 1) {
         // ------------------------- raw weight chunk producer ----------------------------
         // A thread of its own, so that waiting for a raw slot never holds up
         // the x16 stream.
@@ -406,8 +419,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             int r_issued = 0;
             auto issue_raw = [&](int ci) {  // the ci-th chunk of this CTA's sequence
                 const int sr = ci % SR;
-                mbar_arrive_expect_tx(&rfull[sr], (uint32_t)(BN * PITCH));
-                tma_load_2d(sR + sr * BN * PITCH, &a.tmap_w, chunk_of(ci) * 8 * block_bytes(QT) / 4, n0, &rfull[sr]);
+                mbar_arrive_expect_tx(&rfull[sr], (uint32_t)(W * PITCH));
+                tma_load_2d(sR + sr * W * PITCH, &a.tmap_w, chunk_of(ci) * 8 * block_bytes(QT) / 4, n0, &rfull[sr]);
             };
             // immutable weights: the first chunks may load before the dependency wait
             if (a.weights_immutable)
@@ -431,13 +444,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     !mbar_wait_bounded(&full_b[sb], (i / SB) & 1, a.err))
                     break;
                 tc_fence_after();
-                const uint64_t bd = sw128_desc(smem_u32(sB + sb * kTileBytes));
+                const uint64_t bd = sw128_desc(smem_u32(sB + sb * kBTile));
 #pragma unroll
                 for (int t = 0; t < T; ++t) {
                     const uint64_t ad = sw128_desc(smem_u32(sA + (sa * T + t) * kTileBytes));
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)  // 32-byte steps inside the swizzle atom
-                        mma_f16_ss(tmem + t * BN, ad + 2 * k, bd + 2 * k, kIdesc, (i | k) != 0 ? 1u : 0u);
+                        mma_f16_ss(tmem + t * W, ad + 2 * k, bd + 2 * k, gemm_idesc(W), (i | k) != 0 ? 1u : 0u);
                 }
                 // both stages are free once these MMAs have read them
                 mma_commit(&empty_a[sa]);
@@ -449,8 +462,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     } else {
         // --------------------- dequantisers, then the epilogue (warps 2-9) ----------------
         const int d = threadIdx.x - 64;
-        const int row = d & (BN - 1);  // weight row inside the tile
-        const int blk = d >> 7;        // which block of the K step (warp-uniform)
+        const int row = d % W;  // weight row inside the tile
+        const int blk = d / W;  // which block of the K step (warp-uniform: W is a multiple of 32)
         const int r7 = row & 7;
         pdl_wait();
         bool ok = true;
@@ -458,8 +471,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             constexpr int KK = decltype(kk)::value;
             const int s = i % SB;
             if (i >= SB && !mbar_wait_bounded(&empty_b[s], ((i / SB) - 1) & 1, a.err)) return false;
-            const uint8_t* rrow = sR + sr * BN * PITCH + row * PITCH;
-            uint8_t* dst = sB + s * kTileBytes + (row >> 3) * 1024 + r7 * 128;
+            const uint8_t* rrow = sR + sr * W * PITCH + row * PITCH;
+            uint8_t* dst = sB + s * kBTile + (row >> 3) * 1024 + r7 * 128;
             if (blk == 0)
                 dequant_kstep<QT, KK, 0>(rrow, dst, r7);
             else
@@ -484,17 +497,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         // operand rings -> whole output rows, 512 coalesced bytes per warp store.
         const bool acc_ok = mbar_wait_bounded(acc_full, 0, a.err);
         tc_fence_after();
-        const int q = warp & 3;            // this warp's TMEM lane quarter
-        const int half = (warp - 2) >> 2;  // two warps per quarter split the columns
-        constexpr int YP = BN + 4;         // staging pitch in floats: 16-byte stores conflict free
+        const int q = warp & 3;  // this warp's TMEM lane quarter
+        // the warps of a quarter (2 or 3) split its 32-column blocks
+        const int qfirst = 2 + ((q - 2) & 3);
+        const int jq = (warp - qfirst) >> 2;
+        const int nq = (2 + kDqWarps - qfirst + 3) >> 2;
+        constexpr int YP = W + 4;  // staging pitch in floats: 16-byte stores conflict free
         float* ys = reinterpret_cast<float*>(sA);
 #pragma unroll
         for (int t = 0; t < T; ++t) {
             const int r = t * BM + q * 32 + lane;  // token row inside the tile
 #pragma unroll 1
-            for (int cb = half; cb < BN / 32; cb += 2) {
+            for (int cb = jq; cb < W / 32; cb += nq) {
                 uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * BN + cb * 32), v);
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * W + cb * 32), v);
                 float4* dstp = reinterpret_cast<float4*>(ys + r * YP + cb * 32);
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
@@ -507,11 +523,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         if (a.gact >= 0) {
             // gate/up weight: tile columns [32j, 32j + 16) are gate rows
             // n0 / 2 + 16j + [0, 16), the next 16 columns the matching up rows;
-            // lanes 0-15 each produce four consecutive outputs
-            const int c = 32 * (lane >> 2) + 4 * (lane & 3);
-            const int64_t i0 = (int64_t)(n0 / 2) + 16 * (lane >> 2) + 4 * (lane & 3);
+            // index li = lane (+32) produces four consecutive outputs
             const bool gvec = ((reinterpret_cast<uintptr_t>(a.gout) & 15) == 0) && (a.ghidden % 4 == 0);
-            for (int r = warp - 2; r < T * BM && acc_ok && lane < 16; r += kDqWarps) {
+            for (int li = lane; li < W / 8; li += 32)
+            for (int r = warp - 2; r < T * BM && acc_ok; r += kDqWarps) {
+                const int c = 32 * (li >> 2) + 4 * (li & 3);
+                const int64_t i0 = (int64_t)(n0 / 2) + 16 * (li >> 2) + 4 * (li & 3);
                 const int m = m0 + r;
                 if (m >= a.M) break;
                 const float sc = a.xs[m];
@@ -533,12 +550,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             }
         }
         const bool vec = ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) && (a.N % 4 == 0);
-        const int n = n0 + 4 * lane;
+        for (int c4 = lane; c4 < W / 4; c4 += 32)
         for (int r = warp - 2; r < T * BM && acc_ok && a.gact < 0; r += kDqWarps) {
+            const int n = n0 + 4 * c4;
             const int m = m0 + r;
             if (m >= a.M) break;  // rows are in increasing order
             const float sc = a.xs[m];
-            const float4 v = *reinterpret_cast<const float4*>(ys + r * YP + 4 * lane);
+            const float4 v = *reinterpret_cast<const float4*>(ys + r * YP + 4 * c4);
             float* yr = a.y + (int64_t)m * a.N + n;
             if (vec && n + 3 < a.N) {
                 *reinterpret_cast<float4*>(yr) = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
@@ -553,18 +571,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, T * BN);
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
 template <int QT>
-const void* pick_t(int T) {
-    return T == 1 ? (const void*)gemm_kernel<QT, 1> : (const void*)gemm_kernel<QT, 2>;
+const void* pick_t(int T, int W) {
+    if (W == 160) return T == 1 ? (const void*)gemm_kernel<QT, 1, 160> : (const void*)gemm_kernel<QT, 2, 160>;
+    return T == 1 ? (const void*)gemm_kernel<QT, 1, BN> : (const void*)gemm_kernel<QT, 2, BN>;
 }
-const void* gemm_kernel_for(int qt, int T) {
-    if (qt == kQ8_0) return pick_t<kQ8_0>(T);
-    if (qt == kQ4_0) return pick_t<kQ4_0>(T);
-    return pick_t<kQ4_1>(T);
+const void* gemm_kernel_for(int qt, int T, int W) {
+    if (qt == kQ8_0) return pick_t<kQ8_0>(T, BN);
+    if (qt == kQ4_0) return pick_t<kQ4_0>(T, W);
+    return pick_t<kQ4_1>(T, W);
 }
 
 cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
@@ -608,8 +627,23 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     cudaError_t e = encode_map_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, (uint64_t)K, (uint64_t)M,
                                   (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
+    // two token tiles per CTA once M needs more than one: each dequantised
+    // weight tile then feeds twice the tensor work
+    const int T = M > BM ? 2 : 1;
+    // weight-tile width: 128 or (Q4_0, Q4_1) 160 rows, whichever needs fewer
+    // rounds of CTAs times rows per CTA (config 3: 172 CTAs of 128 rows are
+    // two waves on 148 SMs, 138 of 160 rows one)
+    int W = BN;
+    if (qt != kQ8_0) {
+        int sms = 148, dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const long gy = (M + T * BM - 1) / (T * BM);
+        const long c128 = ((N + 127) / 128 * gy + sms - 1) / sms * 128;
+        const long c160 = ((N + 159) / 160 * gy + sms - 1) / sms * 160;
+        if (c160 < c128) W = 160;
+    }
     e = encode_map_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, (uint64_t)row_bytes / 4, (uint64_t)N,
-                      (uint64_t)row_bytes, (uint32_t)raw_pitch(qt) / 4, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                      (uint64_t)row_bytes, (uint32_t)raw_pitch(qt) / 4, (uint32_t)W, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (e != cudaSuccess) return e;
     a.xs = xs;
     a.y = y;
@@ -622,15 +656,12 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     a.gact = g.act;
     a.gout = g.out;
     a.ghidden = g.hidden;
-    // two token tiles per CTA once M needs more than one: each dequantised
-    // weight tile then feeds twice the tensor work
-    const int T = M > BM ? 2 : 1;
-    const void* fn = gemm_kernel_for(qt, T);
-    const size_t smem = gemm_smem_bytes(qt, T);
+    const void* fn = gemm_kernel_for(qt, T, W);
+    const size_t smem = gemm_smem_bytes(qt, T, W);
     e = ensure_dynamic_smem(fn, smem);
     if (e != cudaSuccess) return e;
     void* args[] = {(void*)&a};
-    return launch_ex(fn, dim3((N + BN - 1) / BN, (M + T * BM - 1) / (T * BM)), dim3(kGemmThreads), smem, st, args);
+    return launch_ex(fn, dim3((N + W - 1) / W, (M + T * BM - 1) / (T * BM)), dim3(gemm_threads(W)), smem, st, args);
 }
 
 }  // namespace qmm

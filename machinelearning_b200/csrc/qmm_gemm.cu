@@ -65,7 +65,7 @@ constexpr uint32_t kTileBytes = BM * BK * 2;  // 16 KB: 128 rows x 128 bytes (x1
 // that read it have completed -- while dequantised weight tiles (B) are ready
 // ~0.3 us after their raw chunk is. Sized to fill 227 KB with the raw ring.
 __host__ __device__ constexpr int a_stages(int qt, int T, int W = BN) {
-    return T == 1 ? 6 : (W > BN ? 3 : (qt == kQ8_0 ? 3 : 4));
+    return W > 160 ? 4 : (T == 1 ? 6 : (W > BN ? 3 : (qt == kQ8_0 ? 3 : 4)));
 }
 __host__ __device__ constexpr int b_stages(int, int) { return 3; }
 
@@ -94,7 +94,9 @@ __host__ __device__ constexpr size_t gemm_smem_bytes(int qt, int T, int W) {
 }
 static_assert(gemm_smem_bytes(kQ4_0, 2, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 2, 160) <= 232448 &&
                   gemm_smem_bytes(kQ4_0, 1, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 1, 160) <= 232448 &&
-                  gemm_smem_bytes(kQ8_0, 2, BN) <= 232448 && gemm_smem_bytes(kQ4_1, 2, BN) <= 232448,
+                  gemm_smem_bytes(kQ8_0, 2, BN) <= 232448 && gemm_smem_bytes(kQ4_1, 2, BN) <= 232448 &&
+                  gemm_smem_bytes(kQ4_0, 1, 224) <= 232448 && gemm_smem_bytes(kQ4_1, 1, 224) <= 232448 &&
+                  gemm_smem_bytes(kQ8_0, 1, 64) <= 232448 && gemm_smem_bytes(kQ8_0, 2, 64) <= 232448,
               "a GEMM variant exceeds 227 KB of shared memory");
 
 // ---- tcgen05 / TMEM --------------------------------------------------------------
@@ -577,13 +579,25 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
 
 template <int QT>
 const void* pick_t(int T, int W) {
-    if (W == 160) return T == 1 ? (const void*)gemm_kernel<QT, 1, 160> : (const void*)gemm_kernel<QT, 2, 160>;
+    if (W == 64) return T == 1 ? (const void*)gemm_kernel<QT, 1, 64> : (const void*)gemm_kernel<QT, 2, 64>;
+    if constexpr (QT != kQ8_0) {
+        if (W == 160) return T == 1 ? (const void*)gemm_kernel<QT, 1, 160> : (const void*)gemm_kernel<QT, 2, 160>;
+        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224>;
+    }
     return T == 1 ? (const void*)gemm_kernel<QT, 1, BN> : (const void*)gemm_kernel<QT, 2, BN>;
 }
 const void* gemm_kernel_for(int qt, int T, int W) {
-    if (qt == kQ8_0) return pick_t<kQ8_0>(T, BN);
+    if (qt == kQ8_0) return pick_t<kQ8_0>(T, W);
     if (qt == kQ4_0) return pick_t<kQ4_0>(T, W);
     return pick_t<kQ4_1>(T, W);
+}
+
+// Weight-tile widths a call may use: 64, 128, 160 and (one token tile) 224
+// rows for Q4_0 / Q4_1; 64 and 128 for Q8_0 (its raw chunks are twice as wide).
+bool gemm_width_ok(int qt, int T, int W) {
+    if (W == 64 || W == BN) return true;
+    if (qt == kQ8_0) return false;
+    return W == 160 || (W == 224 && T == 1);
 }
 
 cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
@@ -630,17 +644,26 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     // two token tiles per CTA once M needs more than one: each dequantised
     // weight tile then feeds twice the tensor work
     const int T = M > BM ? 2 : 1;
-    // weight-tile width: 128 or (Q4_0, Q4_1) 160 rows, whichever needs fewer
-    // rounds of CTAs times rows per CTA (config 3: 172 CTAs of 128 rows are
-    // two waves on 148 SMs, 138 of 160 rows one)
+    // Weight-tile width: the fewest rounds of CTAs (waves on the SMs) times
+    // the time per K step, which depends little on the width (measured on
+    // B200: ~0.33 + 0.0011 W us per K step for W = 64..224). Config 3: 138
+    // CTAs of 160 rows (one wave) instead of 172 of 128 (two): 95 -> 52 us;
+    // Llama gate at M = 32: 128 CTAs of 224 rows instead of 224 of 128.
     int W = BN;
-    if (qt != kQ8_0) {
+    {
         int sms = 148, dev = 0;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const long gy = (M + T * BM - 1) / (T * BM);
-        const long c128 = ((N + 127) / 128 * gy + sms - 1) / sms * 128;
-        const long c160 = ((N + 159) / 160 * gy + sms - 1) / sms * 160;
-        if (c160 < c128) W = 160;
+        long best = -1;
+        for (const int w : {64, 128, 160, 224}) {
+            if (!gemm_width_ok(qt, T, w)) continue;
+            const long rounds = ((N + w - 1) / w * gy + sms - 1) / sms;
+            const long cost = rounds * (300 + w);
+            if (best < 0 || cost < best) {
+                best = cost;
+                W = w;
+            }
+        }
     }
     e = encode_map_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, (uint64_t)row_bytes / 4, (uint64_t)N,
                       (uint64_t)row_bytes, (uint32_t)raw_pitch(qt) / 4, (uint32_t)W, CU_TENSOR_MAP_SWIZZLE_NONE);

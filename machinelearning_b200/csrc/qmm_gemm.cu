@@ -81,6 +81,9 @@ struct GArgs {
     float* y;
     int M, N, K, ksteps, weights_immutable;
     int* err;
+    int ks, cps;         // K slices (blockIdx.z) and raw chunks per slice
+    float* partial;      // [ks][M][N] unscaled partial tiles (ks > 1)
+    unsigned* counters;  // [tiles] tickets, zero before the launch (ks > 1)
     int gact;        // >= 0: gate/up epilogue (GatedOut), y unused
     float* gout;     // [M][ghidden]
     int64_t ghidden;
@@ -350,13 +353,17 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * W, m0 = blockIdx.y * (T * BM);
-    const int nchunks = (a.ksteps + kStepsPerChunk - 1) / kStepsPerChunk;
+    // K slice blockIdx.z: raw chunks [c_begin, c_begin + nchunks) of the rows
+    const int nchunks_all = (a.ksteps + kStepsPerChunk - 1) / kStepsPerChunk;
+    const int c_begin = (int)blockIdx.z * a.cps;
+    const int nchunks = max(1, min(nchunks_all - c_begin, a.cps));  // the planner gives every slice a chunk
+    const int steps = min(a.ksteps, (c_begin + nchunks) * kStepsPerChunk) - c_begin * kStepsPerChunk;
     // Every CTA starts its K loop at a different raw chunk: CTAs that share a
     // token tile then fetch different x16 tiles at any moment instead of all
     // hitting the same L2 lines (the sum order differs per tile, results stay
     // deterministic).
     const int rot = (int)(blockIdx.x % (unsigned)nchunks);
-    auto chunk_of = [&](int ci) { return ci + rot < nchunks ? ci + rot : ci + rot - nchunks; };
+    auto chunk_of = [&](int ci) { return c_begin + (ci + rot < nchunks ? ci + rot : ci + rot - nchunks); };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SA; ++s) {
@@ -440,7 +447,7 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         // ------------------------------- MMA issuer -----------------------------------
         if (lane == 0) {
             pdl_wait();
-            for (int i = 0; i < a.ksteps; ++i) {  // operand steps in this CTA's chunk order
+            for (int i = 0; i < steps; ++i) {  // operand steps in this CTA's chunk order
                 const int sa = i % SA, sb = i % SB;
                 if (!mbar_wait_bounded(&full_a[sa], (i / SA) & 1, a.err) ||
                     !mbar_wait_bounded(&full_b[sb], (i / SB) & 1, a.err))
@@ -522,13 +529,59 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         }
         tc_fence_before();
         asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");  // the staging tile is complete
+        bool store = acc_ok;
+        if (a.ks > 1) {
+            // K split: this slice's unscaled tile to the workspace; the last slice
+            // of the tile to arrive rebuilds the staging tile as the sum of all
+            // slices in slice order, then stores it like an unsplit tile
+            const int et = threadIdx.x - 64;  // 0 .. kDqThreads - 1
+            float* mine = a.partial + (int64_t)blockIdx.z * a.M * a.N;
+            for (int c4 = lane; c4 < W / 4; c4 += 32)
+                for (int r = warp - 2; r < T * BM; r += kDqWarps) {
+                    const int m = m0 + r, n = n0 + 4 * c4;
+                    if (m >= a.M) break;
+                    const float4 v = *reinterpret_cast<const float4*>(ys + r * YP + 4 * c4);
+                    float* pr = mine + (int64_t)m * a.N + n;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (n + e < a.N) pr[e] = (&v.x)[e];
+                }
+            __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");
+            uint32_t* flag = tmem_slot + 1;
+            const unsigned tile = blockIdx.y * gridDim.x + blockIdx.x;
+            if (et == 0) {
+                const unsigned t = atomicAdd(&a.counters[tile], 1u);
+                *flag = (t == (unsigned)(a.ks - 1)) ? 1u : 0u;
+                if (t == (unsigned)(a.ks - 1)) a.counters[tile] = 0u;  // left zero for the next call
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");
+            store = store && *flag != 0u;
+            if (store) {
+                __threadfence();
+                for (int c4 = lane; c4 < W / 4; c4 += 32)
+                    for (int r = warp - 2; r < T * BM; r += kDqWarps) {
+                        const int m = m0 + r, n = n0 + 4 * c4;
+                        if (m >= a.M) break;
+                        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        for (int q = 0; q < a.ks; ++q) {
+                            const float* pq = a.partial + ((int64_t)q * a.M + m) * a.N + n;
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                if (n + e < a.N) acc[e] += __ldcg(pq + e);
+                        }
+                        *reinterpret_cast<float4*>(ys + r * YP + 4 * c4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                    }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");
+        }
         if (a.gact >= 0) {
             // gate/up weight: tile columns [32j, 32j + 16) are gate rows
             // n0 / 2 + 16j + [0, 16), the next 16 columns the matching up rows;
             // index li = lane (+32) produces four consecutive outputs
             const bool gvec = ((reinterpret_cast<uintptr_t>(a.gout) & 15) == 0) && (a.ghidden % 4 == 0);
             for (int li = lane; li < W / 8; li += 32)
-            for (int r = warp - 2; r < T * BM && acc_ok; r += kDqWarps) {
+            for (int r = warp - 2; r < T * BM && store; r += kDqWarps) {
                 const int c = 32 * (li >> 2) + 4 * (li & 3);
                 const int64_t i0 = (int64_t)(n0 / 2) + 16 * (li >> 2) + 4 * (li & 3);
                 const int m = m0 + r;
@@ -553,7 +606,7 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         }
         const bool vec = ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) && (a.N % 4 == 0);
         for (int c4 = lane; c4 < W / 4; c4 += 32)
-        for (int r = warp - 2; r < T * BM && acc_ok && a.gact < 0; r += kDqWarps) {
+        for (int r = warp - 2; r < T * BM && store && a.gact < 0; r += kDqWarps) {
             const int n = n0 + 4 * c4;
             const int m = m0 + r;
             if (m >= a.M) break;  // rows are in increasing order
@@ -625,7 +678,56 @@ bool gemm_supported(int qt, bool native, int M, int N, int K) {
     return row_bytes % 16 == 0;  // 2-D TMA boxes of the raw rows
 }
 
-size_t gemm_workspace_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((size_t)M * 4); }
+namespace {
+// Launch shape of a call: token tiles per CTA, weight-tile width, K slices and
+// raw chunks per slice. The fewest rounds of CTAs (waves on the SMs) times the
+// K steps a CTA runs times the time per K step, which depends little on the
+// width (measured on B200: ~0.33 + 0.0011 W us per K step for W = 64..224).
+// Config 3: 138 CTAs of 160 rows (one wave) instead of 172 of 128: 95 ->
+// 52 us; Llama gate at M = 32: 128 CTAs of 224 rows instead of 224 of 128;
+// Llama down at M = 32 (448 K steps): 37 tiles of 224 rows x 4 K slices.
+struct GemmPlan {
+    int T, W, ks, cps;
+};
+GemmPlan gemm_plan(int qt, int M, int N, int K) {
+    GemmPlan p{M > BM ? 2 : 1, BN, 1, 0};
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int ksteps = (K + BK - 1) / BK;
+    const int nch = (ksteps + kStepsPerChunk - 1) / kStepsPerChunk;
+    p.cps = nch;
+    const long gy = (M + p.T * BM - 1) / (p.T * BM);
+    double best = -1.0;
+    for (const int w : {64, 128, 160, 224}) {
+        if (!gemm_width_ok(qt, p.T, w)) continue;
+        for (int ks = 1; ks <= 4; ks *= 2) {
+            const int cps = (nch + ks - 1) / ks;
+            if ((nch + cps - 1) / cps != ks) continue;  // every slice gets a chunk
+            const long rounds = ((N + w - 1) / w * gy * ks + sms - 1) / sms;
+            const int steps = min(ksteps, cps * kStepsPerChunk);
+            const double cost = (double)rounds * steps * (300 + w) * (ks > 1 ? 1.03 : 1.0);
+            if (best < 0.0 || cost < best) {
+                best = cost;
+                p.W = w;
+                p.ks = ks;
+                p.cps = cps;
+            }
+        }
+    }
+    return p;
+}
+size_t x16_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((size_t)M * 4); }
+}  // namespace
+
+size_t gemm_workspace_bytes(int M, int N, int K, int qt) {
+    const GemmPlan p = gemm_plan(qt, M, N, K);
+    size_t b = x16_bytes(M, K);
+    if (p.ks > 1) {
+        const long tiles = (long)((N + p.W - 1) / p.W) * ((M + p.T * BM - 1) / (p.T * BM));
+        b += align256((size_t)p.ks * M * N * 4) + align256((size_t)tiles * 4);
+    }
+    return b;
+}
 
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws, int* err,
                         cudaStream_t st, bool weights_immutable, const GatedOut& g) {
@@ -641,29 +743,19 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     cudaError_t e = encode_map_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, (uint64_t)K, (uint64_t)M,
                                   (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
-    // two token tiles per CTA once M needs more than one: each dequantised
-    // weight tile then feeds twice the tensor work
-    const int T = M > BM ? 2 : 1;
-    // Weight-tile width: the fewest rounds of CTAs (waves on the SMs) times
-    // the time per K step, which depends little on the width (measured on
-    // B200: ~0.33 + 0.0011 W us per K step for W = 64..224). Config 3: 138
-    // CTAs of 160 rows (one wave) instead of 172 of 128 (two): 95 -> 52 us;
-    // Llama gate at M = 32: 128 CTAs of 224 rows instead of 224 of 128.
-    int W = BN;
-    {
-        int sms = 148, dev = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const long gy = (M + T * BM - 1) / (T * BM);
-        long best = -1;
-        for (const int w : {64, 128, 160, 224}) {
-            if (!gemm_width_ok(qt, T, w)) continue;
-            const long rounds = ((N + w - 1) / w * gy + sms - 1) / sms;
-            const long cost = rounds * (300 + w);
-            if (best < 0 || cost < best) {
-                best = cost;
-                W = w;
-            }
-        }
+    const GemmPlan gp = gemm_plan(qt, M, N, K);
+    const int T = gp.T, W = gp.W;
+    const long tiles = (long)((N + W - 1) / W) * ((M + T * BM - 1) / (T * BM));
+    a.ks = gp.ks;
+    a.cps = gp.cps;
+    a.partial = nullptr;
+    a.counters = nullptr;
+    if (gp.ks > 1) {
+        uint8_t* b = static_cast<uint8_t*>(ws) + x16_bytes(M, K);
+        a.partial = reinterpret_cast<float*>(b);
+        a.counters = reinterpret_cast<unsigned*>(b + align256((size_t)gp.ks * M * N * 4));
+        e = cudaMemsetAsync(a.counters, 0, (size_t)tiles * 4, st);  // the tickets start from zero
+        if (e != cudaSuccess) return e;
     }
     e = encode_map_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, (uint64_t)row_bytes / 4, (uint64_t)N,
                       (uint64_t)row_bytes, (uint32_t)raw_pitch(qt) / 4, (uint32_t)W, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -684,7 +776,8 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     e = ensure_dynamic_smem(fn, smem);
     if (e != cudaSuccess) return e;
     void* args[] = {(void*)&a};
-    return launch_ex(fn, dim3((N + W - 1) / W, (M + T * BM - 1) / (T * BM)), dim3(gemm_threads(W)), smem, st, args);
+    return launch_ex(fn, dim3((N + W - 1) / W, (M + T * BM - 1) / (T * BM), gp.ks), dim3(gemm_threads(W)), smem,
+                     st, args);
 }
 
 }  // namespace qmm

@@ -206,8 +206,10 @@ cudaError_t encode_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const voi
 // and a weight row pitch that is a multiple of 16 bytes.
 constexpr int kGemmMinRows = 17;
 bool gemm_supported(int qt, bool native, int M, int N, int K);
-size_t gemm_workspace_bytes(int M, int K);
-// ws: gemm_workspace_bytes(M, K) bytes, 256-byte aligned.
+// x16 activations and scales, plus K-slice partials and tickets when the call's
+// plan splits K (planned per device the same way at launch).
+size_t gemm_workspace_bytes(int M, int N, int K, int qt);
+// ws: gemm_workspace_bytes(M, N, K, qt) bytes, 256-byte aligned.
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
                         int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut());
 

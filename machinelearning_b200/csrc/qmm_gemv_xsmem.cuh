@@ -55,6 +55,112 @@ __device__ __forceinline__ int frexp_exponent(float a) {
     return (31 - __clz(bits)) - 148;  // subnormal: highest set mantissa bit
 }
 
+// One (block, token) task of the activation preparation below, spread over
+// LPT consecutive lanes: lane q of the task holds elements [q*32/LPT,
+// (q+1)*32/LPT) -- G = 8/LPT groups of four. The block maximum and the
+// correction sum use the lanes' local values first and shuffles only for the
+// last log2(LPT) levels; the sum keeps the pairwise order
+// ((c0+c1)+(c2+c3))+((c4+c5)+(c6+c7)) over the groups for every LPT, so the
+// records do not depend on LPT. `live` false: the lanes take part in the
+// shuffles (a task's lanes share a warp) but store nothing.
+template <int QT, int LPT>
+__device__ __forceinline__ void prep_x_task(const float* __restrict__ src, bool al16, uint8_t* rec, uint32_t lo_plane,
+                                            uint32_t* r8, int q, bool live) {
+    constexpr int G = 8 / LPT;
+    float v[4 * G];
+    if (al16) {
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+            const float4 f = reinterpret_cast<const float4*>(src)[q * G + j];
+            v[4 * j] = f.x;
+            v[4 * j + 1] = f.y;
+            v[4 * j + 2] = f.z;
+            v[4 * j + 3] = f.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4 * G; ++j) v[j] = src[q * 4 * G + j];
+    }
+    float am = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4 * G; ++j) am = fmaxf(am, fabsf(v[j]));
+#pragma unroll
+    for (int o = 1; o < LPT; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    int e = 0;
+    if (am > 0.0f && am <= 3.402823466e38f) e = max(-126, min(127, frexp_exponent(am) - 14));
+    const float s0 = exp2_int(-e);
+    // record order inside each group of four: Q8_0 (0,1,2,3), Q4 (0,2,1,3)
+    constexpr int P1 = QT == kQ8_0 ? 1 : 2, P2 = QT == kQ8_0 ? 2 : 1;
+    float cg[G], sg[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+        const int gl = q * G + j;    // group: elements 4gl..4gl+3
+        const bool upper = gl >= 4;  // elements 16..31
+        // Q4 formats: high-nibble elements meet weights pre-multiplied by 16
+        // by the magic trick, so their activations are pre-divided by 16.
+        // Multiplying by an exact power of two rounds exactly as ldexpf.
+        const float scale = s0 * ((QT != kQ8_0 && upper) ? 0.0625f : 1.0f);
+        const float coef = QT == kQ8_0 ? 1152.0f : (QT == kQ4_0 ? (upper ? 1152.0f : 1032.0f) : 1024.0f);
+        float vv[4];
+        vv[0] = v[4 * j] * scale;
+        vv[1] = v[4 * j + P1] * scale;
+        vv[2] = v[4 * j + P2] * scale;
+        vv[3] = v[4 * j + 3] * scale;
+        const __half2 h01 = __floats2half2_rn(vv[0], vv[1]), h23 = __floats2half2_rn(vv[2], vv[3]);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        const __half2 l01 = __floats2half2_rn(vv[0] - f01.x, vv[1] - f01.y);
+        const __half2 l23 = __floats2half2_rn(vv[2] - f23.x, vv[3] - f23.y);
+        const float2 g01 = __half22float2(l01), g23 = __half22float2(l23);
+        const float rep[4] = {f01.x + g01.x, f01.y + g01.y, f23.x + g23.x, f23.y + g23.y};
+        cg[j] = coef * rep[0] + coef * rep[1] + coef * rep[2] + coef * rep[3];
+        sg[j] = QT == kQ4_1 ? (rep[0] + rep[1] + rep[2] + rep[3]) * (upper ? 16.0f : 1.0f) : 0.0f;
+        if (live) {
+            // 16-byte record r holds groups r and r + 4, in the hi plane and
+            // in the lo plane
+            uint8_t* rp = rec + 16 * (gl & 3) + (upper ? 8 : 0);
+            *reinterpret_cast<uint2*>(rp) = make_uint2(h2_bits(h01), h2_bits(h23));
+            *reinterpret_cast<uint2*>(rp + lo_plane) = make_uint2(h2_bits(l01), h2_bits(l23));
+        }
+    }
+#pragma unroll
+    for (int w = 1; w < G; w <<= 1)
+#pragma unroll
+        for (int j = 0; j < G; j += 2 * w) {
+            cg[j] = cg[j] + cg[j + w];
+            sg[j] = sg[j] + sg[j + w];
+        }
+    float corr = cg[0], sx = sg[0];
+#pragma unroll
+    for (int o = 1; o < LPT; o <<= 1) {
+        corr += __shfl_xor_sync(0xffffffffu, corr, o);
+        if (QT == kQ4_1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    }
+    if (live && q == 0) {
+        r8[0] = r8[2] = __float_as_uint(-corr);  // the MMA accumulator starts at -corr
+        r8[4] = __float_as_uint(exp2_int(e));
+        r8[6] = __float_as_uint(sx);
+    }
+}
+
+// All tasks (block b, token m) = task b*M + m, nthreads / LPT at a time. A
+// warp past the last task leaves; in the last round, lanes past it shadow the
+// last task without storing (the shuffles need every lane of the warp).
+template <int QT, int LPT>
+__device__ __forceinline__ void prep_x_lanes(const float* __restrict__ x, int M, int K, int kb0, int ntask, bool al16,
+                                             uint8_t* xf, uint32_t lo_plane, uint32_t* side, int npair, int mstride,
+                                             int tid, int nthreads) {
+    const int per = nthreads / LPT;
+    for (int t0 = 0; t0 < ntask; t0 += per) {
+        if (t0 + (tid & ~31) / LPT >= ntask) break;  // warp-uniform
+        const int task = t0 + tid / LPT;
+        const bool live = task < ntask;
+        const int tk = live ? task : ntask - 1;
+        const int b = tk / M, m = tk - b * M;
+        prep_x_task<QT, LPT>(x + (int64_t)m * K + (int64_t)(kb0 + b) * QK, al16, xf + (uint32_t)(b * mstride + m) * 64,
+                             lo_plane, side + (b * npair + (m >> 1)) * 8 + (m & 1), tid % LPT, live);
+    }
+}
+
 // Activation records for blocks [kb0, kb0 + nbc) of x [M][K] (f32), written
 // to shared memory by threads tid = 0..nthreads-1 (a multiple of 32) of the
 // CTA. Per (block, token): scale by 2^-e so max|x| lands in [2^13, 2^14),
@@ -65,107 +171,27 @@ __device__ __forceinline__ int frexp_exponent(float a) {
 // pairs per block (npair >= ceil(M / 2)); tokens M..2*npair-1 get neutral side
 // records. mstride >= M: tokens per block in the xf planes (records of tokens
 // M..mstride-1 are not written). The caller synchronises before reading them.
+// Lanes per task by task count (measured on B200: few tasks want short
+// per-lane chains, many tasks fewer shuffles); the records are the same.
 template <int QT>
 __device__ __forceinline__ void prep_x_smem(const float* __restrict__ x, int M, int K, int kb0, int nbc,
                                             uint8_t* xf, uint32_t lo_plane, uint32_t* side, int npair, int tid,
                                             int nthreads, int mstride = 0) {
     if (mstride < M) mstride = M;
-    const int warp = tid >> 5, lane = tid & 31;
-    {
-        const int npt = 2 * npair - M;  // padding tokens per block: neutral records
-        for (int i = tid; i < nbc * npt; i += nthreads) {
-            const int b = i / npt, m = M + i % npt;
-            uint32_t* r8 = side + (b * npair + (m >> 1)) * 8 + (m & 1);
-            r8[0] = r8[2] = r8[4] = r8[6] = 0u;
-        }
-        const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-        const int ntask = nbc * M;
-        const int gl = lane & 7;         // lane in the 8-lane group: elements 4gl..4gl+3
-        const bool upper = gl >= 4;      // elements 16..31
-        // kPrepUnroll rounds of 32 tasks per pass: their global loads are all
-        // in flight together instead of one L2 round trip per round
-        constexpr int kPrepUnroll = kResidentPrepUnroll;
-        const int kRound = nthreads / 8;
-        for (int base = warp * 4; base < ntask; base += kRound * kPrepUnroll) {  // warp-uniform trip count
-          float vu[kPrepUnroll][4];
-#pragma unroll
-          for (int u = 0; u < kPrepUnroll; ++u) {
-            const int task = base + u * kRound + (lane >> 3);
-            vu[u][0] = vu[u][1] = vu[u][2] = vu[u][3] = 0.0f;
-            if (task < ntask) {
-                const int b = task / M, m = task % M;
-                const float* src = x + (int64_t)m * K + (int64_t)(kb0 + b) * QK + 4 * gl;
-                if (x16) {
-                    const float4 q = *reinterpret_cast<const float4*>(src);
-                    vu[u][0] = q.x;
-                    vu[u][1] = q.y;
-                    vu[u][2] = q.z;
-                    vu[u][3] = q.w;
-                } else {
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) vu[u][r] = src[r];
-                }
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kPrepUnroll; ++u) {
-            if (base + u * kRound >= ntask) break;  // warp-uniform
-            const int task = base + u * kRound + (lane >> 3);
-            const bool live = task < ntask;
-            const int b = live ? task / M : 0;
-            const int m = live ? task % M : 0;
-            const float v[4] = {vu[u][0], vu[u][1], vu[u][2], vu[u][3]};
-            float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
-            int e = 0;
-            if (am > 0.0f && am <= 3.402823466e38f) e = max(-126, min(127, frexp_exponent(am) - 14));
-            // Q4 formats: high-nibble elements meet weights pre-multiplied by 16
-            // by the magic trick, so their activations are pre-divided by 16.
-            // Multiplying by an exact power of two rounds exactly as ldexpf.
-            const float scale = exp2_int(-e) * ((QT != kQ8_0 && upper) ? 0.0625f : 1.0f);
-            const float coef = QT == kQ8_0 ? 1152.0f : (QT == kQ4_0 ? (upper ? 1152.0f : 1032.0f) : 1024.0f);
-            // record order inside each group of four: Q8_0 (0,1,2,3), Q4 (0,2,1,3)
-            constexpr int P1 = QT == kQ8_0 ? 1 : 2, P2 = QT == kQ8_0 ? 2 : 1;
-            float vv[4];
-            vv[0] = v[0] * scale;
-            vv[1] = v[P1] * scale;
-            vv[2] = v[P2] * scale;
-            vv[3] = v[3] * scale;
-            const __half2 h01 = __floats2half2_rn(vv[0], vv[1]), h23 = __floats2half2_rn(vv[2], vv[3]);
-            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-            const __half2 l01 = __floats2half2_rn(vv[0] - f01.x, vv[1] - f01.y);
-            const __half2 l23 = __floats2half2_rn(vv[2] - f23.x, vv[3] - f23.y);
-            const float2 g01 = __half22float2(l01), g23 = __half22float2(l23);
-            const float rep[4] = {f01.x + g01.x, f01.y + g01.y, f23.x + g23.x, f23.y + g23.y};
-            float corr = coef * rep[0] + coef * rep[1] + coef * rep[2] + coef * rep[3];
-            float sx = 0.0f;
-            if (QT == kQ4_1) sx = (rep[0] + rep[1] + rep[2] + rep[3]) * (upper ? 16.0f : 1.0f);
-            corr += __shfl_xor_sync(0xffffffffu, corr, 1);
-            corr += __shfl_xor_sync(0xffffffffu, corr, 2);
-            corr += __shfl_xor_sync(0xffffffffu, corr, 4);
-            if (QT == kQ4_1) {
-                sx += __shfl_xor_sync(0xffffffffu, sx, 1);
-                sx += __shfl_xor_sync(0xffffffffu, sx, 2);
-                sx += __shfl_xor_sync(0xffffffffu, sx, 4);
-            }
-            if (live) {
-                // thread t's 16-byte record holds elements 4t..4t+3 then
-                // 16+4t..16+4t+3, in the hi plane and in the lo plane
-                uint8_t* rec = xf + ((uint32_t)(b * mstride + m) * 4 + (gl & 3)) * 16 + (upper ? 8 : 0);
-                *reinterpret_cast<uint2*>(rec) = make_uint2(h2_bits(h01), h2_bits(h23));
-                *reinterpret_cast<uint2*>(rec + lo_plane) = make_uint2(h2_bits(l01), h2_bits(l23));
-                if (gl == 0) {
-                    uint32_t* r8 = side + (b * npair + (m >> 1)) * 8 + (m & 1);
-                    r8[0] = r8[2] = __float_as_uint(-corr);  // the MMA accumulator starts at -corr
-                    r8[4] = __float_as_uint(exp2_int(e));
-                    r8[6] = __float_as_uint(sx);
-                }
-            }
-          }
-        }
+    const int npt = 2 * npair - M;  // padding tokens per block: neutral records
+    for (int i = tid; i < nbc * npt; i += nthreads) {
+        const int b = i / npt, m = M + i % npt;
+        uint32_t* r8 = side + (b * npair + (m >> 1)) * 8 + (m & 1);
+        r8[0] = r8[2] = r8[4] = r8[6] = 0u;
     }
+    const bool al16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;  // K * 4 is a multiple of 128
+    const int ntask = nbc * M;
+    if (ntask <= 32)
+        prep_x_lanes<QT, 8>(x, M, K, kb0, ntask, al16, xf, lo_plane, side, npair, mstride, tid, nthreads);
+    else if (M == 1 && ntask <= 160)
+        prep_x_lanes<QT, 4>(x, M, K, kb0, ntask, al16, xf, lo_plane, side, npair, mstride, tid, nthreads);
+    else
+        prep_x_lanes<QT, 2>(x, M, K, kb0, ntask, al16, xf, lo_plane, side, npair, mstride, tid, nthreads);
 }
 
 }  // namespace qmm

@@ -499,7 +499,7 @@ bool resident_plan(GemvPlan& q, int num_sms) {
     const int G = (q.nb + kChunk - 1) / kChunk;
     double best = 0.0;
     bool found = false;
-    for (int C = 1; C <= 8 && C <= G; C *= 2) {
+    for (int C = 1; C <= kMaxResidentCluster && C <= G; C *= 2) {
         const int gpc = (G + C - 1) / C;
         const int nbc = q.nb < gpc * kChunk ? q.nb : gpc * kChunk;
         for (int tw = 1; tw <= kW; tw *= 2) {

@@ -194,13 +194,25 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
             if (n < a.N) a.y[(int64_t)m * a.N + n] = s;
         }
     };
+    const int osh = gated ? 4 : 5;  // log2(orows)
     for (int o = threadIdx.x; o < nout; o += kThreads) {
-        const int row = o % orows, m = (o / orows) % a.M, tl2 = o / (orows * a.M);
+        const int row = o & (orows - 1), mt = o >> osh;
+        const int tl2 = mt / a.M, m = mt - tl2 * a.M;
+        // the warps' partials: all loads first, then the sum in warp order
+        const float* pp = part + ((tl2 * wpt * NT + (m >> 3)) * kRows + row) * 8 + (m & 7);
+        float pv[kW], pu[kW];
+#pragma unroll
+        for (int q = 0; q < kW; ++q) {
+            pv[q] = q < wpt ? pp[q * NT * kRows * 8] : 0.0f;
+            pu[q] = (gated && q < wpt) ? pp[q * NT * kRows * 8 + kGateGroup * 8] : 0.0f;
+        }
         float s = 0.0f, su = 0.0f;
-        for (int q = 0; q < wpt; ++q) {
-            const float* pp = part + (((tl2 * wpt + q) * NT + (m >> 3)) * kRows + row) * 8 + (m & 7);
-            s += pp[0];
-            if (gated) su += pp[kGateGroup * 8];
+#pragma unroll
+        for (int q = 0; q < kW; ++q) {
+            if (q < wpt) {
+                s += pv[q];
+                su += pu[q];
+            }
         }
         if (a.cluster == 1) {
             store(tl2, m, row, s, su);
@@ -212,12 +224,24 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_resident_kernel(const __grid
     if (a.cluster > 1) {
         cluster_sync();
         for (int o = rank * kThreads + threadIdx.x; o < nout; o += a.cluster * kThreads) {
-            const int row = o % orows, m = (o / orows) % a.M, tl2 = o / (orows * a.M);
+            const int row = o & (orows - 1), mt = o >> osh;
+            const int tl2 = mt / a.M, m = mt - tl2 * a.M;
             const float* src = cpart + (tl2 * MP + m) * kRows + row;
+            // the cluster's partials (at most kMaxResidentCluster): all remote
+            // loads in flight together, then the sum in rank order
+            float cv[kMaxResidentCluster], cu[kMaxResidentCluster];
+#pragma unroll
+            for (int q = 0; q < kMaxResidentCluster; ++q) {
+                cv[q] = q < a.cluster ? ld_cluster_f32(src, (uint32_t)q) : 0.0f;
+                cu[q] = (gated && q < a.cluster) ? ld_cluster_f32(src + kGateGroup, (uint32_t)q) : 0.0f;
+            }
             float s = 0.0f, su = 0.0f;
-            for (int q = 0; q < a.cluster; ++q) {
-                s += ld_cluster_f32(src, (uint32_t)q);
-                if (gated) su += ld_cluster_f32(src + kGateGroup, (uint32_t)q);
+#pragma unroll
+            for (int q = 0; q < kMaxResidentCluster; ++q) {
+                if (q < a.cluster) {
+                    s += cv[q];
+                    su += cu[q];
+                }
             }
             store(tl2, m, row, s, su);
         }

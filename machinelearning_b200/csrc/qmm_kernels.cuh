@@ -181,6 +181,8 @@ cudaError_t launch_gemv_resident(const GemvPlan& p, const CUtensorMap& tmap, con
 // Activation-prep tasks ((block, token) pairs) a resident CTA handles per pass:
 // 32 eight-lane groups x this many rounds, loads of a pass in flight together.
 constexpr int kResidentPrepUnroll = 8;
+// Largest cluster the resident-kernel planner uses (CTAs summed through DSMEM).
+constexpr int kMaxResidentCluster = 8;
 
 // How many resident-kernel clusters of `cluster` CTAs (CTAs, for cluster 1)
 // with `smem` bytes of shared memory can be resident on the current device at

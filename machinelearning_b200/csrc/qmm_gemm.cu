@@ -65,9 +65,11 @@ constexpr uint32_t kTileBytes = BM * BK * 2;  // 16 KB: 128 rows x 128 bytes (x1
 // that read it have completed -- while dequantised weight tiles (B) are ready
 // ~0.3 us after their raw chunk is. Sized to fill 227 KB with the raw ring.
 __host__ __device__ constexpr int a_stages(int qt, int T, int W = BN) {
-    return W > 160 ? 4 : (T == 1 ? 6 : (W > BN ? 3 : (qt == kQ8_0 ? 3 : 4)));
+    return W > 160 ? (qt == kQ8_0 ? 3 : 4) : (T == 1 ? 6 : (W > BN ? 3 : (qt == kQ8_0 ? 3 : 4)));
 }
-__host__ __device__ constexpr int b_stages(int, int) { return 3; }
+// Q8_0 at 224 rows: its raw chunks (272-byte rows) leave room for two
+// dequantised tiles only.
+__host__ __device__ constexpr int b_stages(int qt, int, int W = BN) { return (qt == kQ8_0 && W > 160) ? 2 : 3; }
 
 // Raw chunk row pitch in shared memory (= the TMA box's inner extent): 8
 // blocks, padded so consecutive rows sit an odd number of 16-byte units apart
@@ -92,14 +94,15 @@ struct GArgs {
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 __host__ __device__ constexpr size_t gemm_smem_bytes(int qt, int T, int W) {
-    return 1024 + (size_t)a_stages(qt, T, W) * T * kTileBytes + (size_t)b_stages(qt, T) * W * BK * 2 +
-           (size_t)SR * W * raw_pitch(qt) + (2 * a_stages(qt, T, W) + 2 * b_stages(qt, T) + 2 * SR + 1) * 8 + 16;
+    return 1024 + (size_t)a_stages(qt, T, W) * T * kTileBytes + (size_t)b_stages(qt, T, W) * W * BK * 2 +
+           (size_t)SR * W * raw_pitch(qt) + (2 * a_stages(qt, T, W) + 2 * b_stages(qt, T, W) + 2 * SR + 1) * 8 + 16;
 }
 static_assert(gemm_smem_bytes(kQ4_0, 2, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 2, 160) <= 232448 &&
                   gemm_smem_bytes(kQ4_0, 1, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 1, 160) <= 232448 &&
                   gemm_smem_bytes(kQ8_0, 2, BN) <= 232448 && gemm_smem_bytes(kQ4_1, 2, BN) <= 232448 &&
                   gemm_smem_bytes(kQ4_0, 1, 224) <= 232448 && gemm_smem_bytes(kQ4_1, 1, 224) <= 232448 &&
-                  gemm_smem_bytes(kQ8_0, 1, 64) <= 232448 && gemm_smem_bytes(kQ8_0, 2, 64) <= 232448,
+                  gemm_smem_bytes(kQ8_0, 1, 64) <= 232448 && gemm_smem_bytes(kQ8_0, 2, 64) <= 232448 &&
+                  gemm_smem_bytes(kQ8_0, 1, 224) <= 232448,
               "a GEMM variant exceeds 227 KB of shared memory");
 
 // ---- tcgen05 / TMEM --------------------------------------------------------------
@@ -332,7 +335,7 @@ __global__ void gemm_xprep_kernel(const float* __restrict__ x, int M, int K, __h
 
 template <int QT, int T, int W>
 __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_constant__ GArgs a) {
-    constexpr int SA = a_stages(QT, T, W), SB = b_stages(QT, T);
+    constexpr int SA = a_stages(QT, T, W), SB = b_stages(QT, T, W);
     constexpr int kDqWarps = dq_warps(W), kDqThreads = dq_threads(W);
     constexpr uint32_t kBTile = (uint32_t)W * BK * 2;  // dequantised weight tile bytes
     constexpr uint32_t kTmemCols = T * W <= 128 ? 128 : (T * W <= 256 ? 256 : 512);
@@ -633,9 +636,9 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
 template <int QT>
 const void* pick_t(int T, int W) {
     if (W == 64) return T == 1 ? (const void*)gemm_kernel<QT, 1, 64> : (const void*)gemm_kernel<QT, 2, 64>;
+    if (W == 224) return (const void*)gemm_kernel<QT, 1, 224>;
     if constexpr (QT != kQ8_0) {
         if (W == 160) return T == 1 ? (const void*)gemm_kernel<QT, 1, 160> : (const void*)gemm_kernel<QT, 2, 160>;
-        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224>;
     }
     return T == 1 ? (const void*)gemm_kernel<QT, 1, BN> : (const void*)gemm_kernel<QT, 2, BN>;
 }
@@ -646,11 +649,11 @@ const void* gemm_kernel_for(int qt, int T, int W) {
 }
 
 // Weight-tile widths a call may use: 64, 128, 160 and (one token tile) 224
-// rows for Q4_0 / Q4_1; 64 and 128 for Q8_0 (its raw chunks are twice as wide).
+// rows for Q4_0 / Q4_1; 64, 128 and (one token tile, shallower rings) 224 for
+// Q8_0 (its raw chunks are twice as wide).
 bool gemm_width_ok(int qt, int T, int W) {
-    if (W == 64 || W == BN) return true;
-    if (qt == kQ8_0) return false;
-    return W == 160 || (W == 224 && T == 1);
+    if (W == 64 || W == BN || (W == 224 && T == 1)) return true;
+    return qt != kQ8_0 && W == 160;
 }
 
 cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {

@@ -172,6 +172,7 @@ GEMM = [
     (Q8_0, 17, 512, 96),
     (Q8_0, 64, 2048, 128),
     (Q8_0, 200, 768, 333),
+    (Q8_0, 20, 544, 33000),  # 224-row tiles (one wave), ragged N and K
     (Q4_1, 40, 384, 130),
     (Q4_1, 300, 1024, 64),
 ]

@@ -485,12 +485,12 @@ bool bank_friendly(int pitch_bytes) { return ((pitch_bytes / 4) & 7) == 4; }
 // two, at most 8), tw 32-row tiles per cluster, shared memory within
 // kResidentSmemMax, and a grid the device can hold in one wave (the runtime's
 // occupancy answer: at most one CTA per SM when it cannot say). Among those,
-// the smallest estimated latency in nanoseconds, from B200 measurements of
-// the kernel's phases: ~110 per block per warp (dependent MMA chains; x1.6
-// for two token tiles), ~1500 per activation-prep pass (a load round trip
-// plus a dependent chain), ~1200 for the cluster exchange (two cluster
-// barriers and the DSMEM sums), and the CTA's weight bytes at ~60 B/ns (the
-// part of the weight fetch the dependency wait does not hide).
+// the smallest estimated latency in nanoseconds, from B200 timestamps of the
+// kernel's phases: ~200 per block per warp (x1.6 for two token tiles), ~500
+// plus ~6.5 per (block, token) task for the activation prep, ~1800 for the
+// cluster exchange (two cluster barriers and the DSMEM sums), and the CTA's
+// weight bytes at ~60 B/ns (the part of the weight fetch the dependency wait
+// does not hide).
 constexpr size_t kResidentSmemMax = 200 * 1024;
 
 bool resident_plan(GemvPlan& q, int num_sms) {
@@ -511,9 +511,8 @@ bool resident_plan(GemvPlan& q, int num_sms) {
             const int wpt = kW / tw;
             const int bpw = (nbc + wpt - 1) / wpt;
             const double wbytes = (double)tw * gpc * kRows * q.pitch;
-            const int passes = (nbc * q.M + 32 * kResidentPrepUnroll - 1) / (32 * kResidentPrepUnroll);
-            const double cost =
-                bpw * 110.0 * (q.nt > 1 ? 1.6 : 1.0) + passes * 1500.0 + (C > 1 ? 1200.0 : 0.0) + wbytes / 60.0;
+            const double cost = bpw * 200.0 * (q.nt > 1 ? 1.6 : 1.0) + (500.0 + 6.5 * nbc * q.M) +
+                                (C > 1 ? 1800.0 : 0.0) + wbytes / 60.0;
             if (!found || cost < best) {
                 found = true;
                 best = cost;

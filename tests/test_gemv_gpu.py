@@ -466,5 +466,23 @@ def test_linear_forward_host_entry(oracle, torch_cuda, qlib):
     qw.close()
 
 
+@pytest.mark.parametrize("m,k,n", [(1, 1152, 256), (8, 6912, 2048), (4, 1024, 5000), (3, 7680, 96)])
+def test_linear_forward_host_pinned(oracle, torch_cuda, qlib, m, k, n):
+    """Pinned host buffers (as a serving loop would pass them) from 1 KB to
+    220 KB, two calls in a row on the library's staging buffers: the oracle's
+    result each time."""
+    from machinelearning_b200.linear import QuantWeight
+    w = make_weights(oracle, Q8_0, n, k, seed=62 + m)
+    qw = QuantWeight.from_host(Q8_0, n, k, w)
+    xn = np.random.default_rng(63 + m).normal(0, 1, m * k).astype(np.float32)
+    x = torch_cuda.from_numpy(xn).pin_memory()
+    y = torch_cuda.full((m * n,), float("nan")).pin_memory()
+    ref = oracle.matmul_f32_q8(xn, w, m, k, n)
+    for _ in range(2):
+        assert qlib.qmm_linear_forward_host(qw.handle, x.data_ptr(), m, y.data_ptr(), 0, None) == 0
+        assert_close_rel(y.numpy(), ref)
+    qw.close()
+
+
 def test_no_device_error_recorded(torch_cuda, qlib):
     assert device_error_clear(qlib) == 0

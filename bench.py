@@ -1,7 +1,8 @@
 """Benchmark of the quantized-matmul hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemma-q8-sweep|q4-gemv|llama70b|llama70b-gate|prefill]
+                    [--workload gemma-q8-sweep|q4-gemv|llama70b|llama70b-gate|prefill|gemma-decode]
+                    [--batch B]
 
 Workloads (synthetic, seeded, weights ~N(0, 0.02)
 quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
@@ -18,6 +19,11 @@ quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
   llama70b-gate (one projection of configs[4]): Q4_0 8192->28672, batch 1,
       two weight copies (264 MB > L2); the small case for streaming-kernel
       profiles.
+  gemma-decode: one full Gemma-3-1B decode step (random init,
+      26 layers, Q4_0 linears, tied Q8_0 lm_head) at position 511 of a
+      512-entry KV cache, batch --batch (1, 16, 64); one CUDA graph replay
+      per step; metric "decode tokens/s" = batch / step time, roofline over
+      the step's weight + KV bytes. N > 1: independent replicas ("weak").
   prefill: Q4_0 [11008 x 4096] x f32 [512 x 4096], one call per
       step on the tensor-core GEMM, six weight copies rotated (152 MB > L2);
       metric "prefill GEMM TFLOP/s" = 2*M*N*K / time, roofline bound "tensor"
@@ -74,6 +80,10 @@ WORKLOADS = {
     "llama70b-gate": dict(
         config_index=4, projections=[("gate", 8192, 28672, Q4_0, "col")], batches=[1], copies=2,
         model="Llama-3-70B FFN gate, Q4_0"),
+    "gemma-decode": dict(
+        config_index=3, projections=[], batches=[1], copies=1, metric="decode",
+        model="Gemma-3-1B architecture, random init: 26 layers, hidden 1152, 4 Q / 1 KV heads of 256, GeGLU 6912, "
+              "vocab 262144 tied; linears Q4_0, lm_head Q8_0; KV context 512"),
     "prefill": dict(
         config_index=2, projections=[("ffn", 4096, 11008, Q4_0, "col")], batches=[512], copies=6,
         model="Llama-7B FFN, Q4_0, 512-token prefill", metric="flops"),
@@ -85,6 +95,8 @@ def metric_info(wl):
     2*M*N*K flops for the prefill GEMM."""
     if wl.get("metric") == "flops":
         return "prefill GEMM TFLOP/s", "TFLOP/s", 1e12
+    if wl.get("metric") == "decode":
+        return "decode tokens/s", "tokens/s", 1.0
     return "quant GEMV HBM GB/s", "GB/s", 1e9
 
 
@@ -593,6 +605,190 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+
+# ---- gemma-decode -------------------------------------------------
+DECODE_POS = 511  # the step attends over the full 512-entry KV context
+
+
+def decode_bytes(cfg, batch, weights_bytes):
+    """HBM bytes one decode step must move: every weight byte once, the KV
+    cache read up to the position (k and v, f32), the gathered embedding rows
+    and the logits written."""
+    kv = cfg.n_layers * batch * cfg.n_kv_heads * (DECODE_POS + 1) * cfg.head_dim * 4 * 2
+    return weights_bytes + kv + batch * (cfg.hidden // 32) * 34 + batch * cfg.vocab * 4
+
+
+def _decode_setup(args, local_rank, rank):
+    import torch
+
+    from machinelearning_b200.decode import Gemma3Config, Gemma3Decoder, random_weights
+    cfg = Gemma3Config.gemma3_1b(ctx=512)
+    w = random_weights(cfg, seed=1234 + rank, device=local_rank)
+    model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank)
+    wbytes = model.emb.nbytes + sum(l[k].nbytes for l in model.layers for k in ("qkv", "o", "gate_up", "down"))
+    return cfg, w, model, wbytes, torch
+
+
+def run_decode(args, rank, world, local_rank):
+    """Decode tokens/s of the Gemma-3-1B step (one graph replay per step at
+    position 511, batch args.batch). N > 1: one independent replica per GPU."""
+    import numpy as np
+    from machinelearning_b200 import _lib
+    cfg, w, model, wbytes, torch = _decode_setup(args, local_rank, rank)
+    L = _lib.lib()
+    dev = model.dev
+    B = args.batch
+    rng = np.random.default_rng(5 + rank)
+    model.set_tokens(rng.integers(0, cfg.vocab, B))
+    model.set_position(DECODE_POS)
+    n0 = L.qmm_launch_count()
+    model.step(advance=False)
+    torch.cuda.synchronize(dev)
+    launches = int(L.qmm_launch_count() - n0)
+    model.capture(advance=False)
+    st = model.stream
+    with torch.cuda.stream(st):
+        for _ in range(args.warmup):
+            model.graph.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank)
+    with sampler:
+        with torch.cuda.stream(st):
+            for _ in range(max(args.warmup, 3)):
+                model.graph.replay()
+        torch.cuda.synchronize(dev)
+        n_before = len(sampler.samples)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            for _ in range(args.steps):
+                model.graph.replay()
+            e1.record(st)
+        torch.cuda.synchronize(dev)
+        n_timed = len(sampler.samples) - n_before
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = B * world * args.steps / (ms / 1e3)
+    step_bytes = decode_bytes(cfg, B, wbytes)
+    achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        # host token ids in, host logits out, every step (pinned buffers)
+        tok_h = torch.as_tensor(rng.integers(0, cfg.vocab, B).astype(np.int32)).pin_memory()
+        log_h = torch.empty(B, cfg.vocab, dtype=torch.float32).pin_memory()
+        k = min(args.steps, 200)
+
+        def e2e_step():
+            with torch.cuda.stream(st):
+                model.tokens.copy_(tok_h, non_blocking=True)
+                model.graph.replay()
+                log_h.copy_(model.logits, non_blocking=True)
+            st.synchronize()
+        for _ in range(3):
+            e2e_step()
+        t0 = time.perf_counter()
+        for _ in range(k):
+            e2e_step()
+        dt_s = time.perf_counter() - t0
+        e2e = {"value": round(B * world * k / dt_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": B * 4,
+               "d2h_bytes_per_step": B * cfg.vocab * 4, "steps": k, "ms_per_step": round(dt_s * 1e3 / k, 4),
+               "path": "pinned host token ids -> graph replay of the decode step -> pinned host logits, synchronous"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = decode_cpu_baseline(cfg, w, B)
+    peak, peak_kind = load_peaks()
+    clocks = sampler.summary()
+    clocks["samples_in_timed_region"] = n_timed
+    model.close()
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 activations and KV cache x Q4_0 linears / Q8_0 lm_head (f16 tensor-core MMA, f32 accumulate)",
+            "data": "synthetic: random-init weights ~N(0,0.02) quantised on device, norm vectors ~N(0,0.1), "
+                    "seeded token ids uniform in the vocabulary",
+            "config": {"workload": args.workload, "baseline_config_index": 3, "model": WORKLOADS["gemma-decode"]["model"],
+                       "batch": B, "position": DECODE_POS, "kv_context": cfg.ctx,
+                       "parallelism": f"{world} replicas" if world > 1 else "single",
+                       "graph": "one CUDA graph per step (embedding, 26 layers, final norm, lm_head)",
+                       "l2": "weights 0.71 GB > L2", "bytes_per_step": step_bytes},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": profiled_traffic(args.workload),
+                         "note": "achieved = weight bytes + KV bytes read + embedding rows + logits per step / step "
+                                 "time (CUDA events on the replay stream)"},
+            "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def _decode_host_weights(w):
+    """The device-quantised weights copied to the host for the CPU oracle."""
+    def h(t):
+        return t.cpu().numpy()
+    return {"emb": h(w["emb"]), "final_norm": h(w["final_norm"]),
+            "layers": [{k: h(v) for k, v in lw.items()} for lw in w["layers"]]}
+
+
+def decode_cpu_time(cfg, hw, batch, steps):
+    import numpy as np
+    import oracle
+    from oracle.decode import decode_step
+    oracle.set_threads(host_cores())
+    kc = [np.zeros((batch, cfg.n_kv_heads, cfg.ctx, cfg.head_dim), np.float32) for _ in range(cfg.n_layers)]
+    vc = [np.zeros_like(kc[0]) for _ in range(cfg.n_layers)]
+    toks = np.random.default_rng(9).integers(0, cfg.vocab, batch)
+    decode_step(cfg, hw, toks, DECODE_POS, kc, vc)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        decode_step(cfg, hw, toks, DECODE_POS, kc, vc)
+    return (time.perf_counter() - t0) / steps
+
+
+def decode_cpu_baseline(cfg, w, batch):
+    import oracle
+    oracle.build()
+    s = decode_cpu_time(cfg, _decode_host_weights(w), batch, 2)
+    return {"value": round(batch / s, 3), "unit": "tokens/s", "cores": oracle.threads(), "kind": "port",
+            "sample": f"2 full decode steps at position {DECODE_POS}, batch {batch}: the oracle's numpy restatement "
+                      "of the reference forward pass with the C++ matmul_f32_q4/_q8 port (AVX2+FMA, OpenMP)"}
+
+
+def run_decode_reference(args, rank, world):
+    """The reference's CPU decode step (oracle restatement) on the same
+    device-generated weights, rank 0 only."""
+    if rank != 0:
+        return
+    import oracle
+    oracle.build()
+    cfg, w, model, wbytes, torch = _decode_setup(args, int(os.environ.get("LOCAL_RANK", "0")), 0)
+    hw = _decode_host_weights(w)
+    model.close()
+    steps = max(1, min(args.steps, 3))
+    s = decode_cpu_time(cfg, hw, args.batch, steps)
+    value = args.batch / s
+    print(json.dumps({
+        "impl": "reference", "metric": "decode tokens/s", "value": round(value, 4), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": round(s * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations and KV cache x Q4_0 / Q8_0 blocks",
+        "data": "synthetic: the same random-init weights, copied to the host",
+        "config": {"workload": args.workload, "baseline_config_index": 3, "batch": args.batch,
+                   "position": DECODE_POS, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": oracle.threads(), "kind": "port",
+                         "sample": f"{steps} full decode steps at position {DECODE_POS}"},
+        "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -603,6 +799,7 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
+    ap.add_argument("--batch", type=int, default=1, help="gemma-decode: sequences per step (1, 16, 64)")
     ap.add_argument("--copies", type=int, default=None,
                     help="weight copies rotated (default: the workload's; fewer for short profiling runs)")
     args = ap.parse_args(argv)
@@ -612,6 +809,25 @@ def main(argv=None):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "gemma-decode":
+        if args.impl == "reference":
+            run_decode_reference(args, rank, world)
+            return 0
+        if world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local_rank))
+        try:
+            run_decode(args, rank, world, local_rank)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+        return 0
     if args.impl == "reference":
         run_reference(args, rank, world)
         return 0

@@ -236,6 +236,50 @@ QMM_API int qmm_dequantize_dev(int dtype, const uint8_t* w_dev, size_t w_len, si
 QMM_API int qmm_gated_act_dev(int act_fn, const float* gate_dev, const float* up_dev, size_t m, size_t hidden,
                               size_t ld, float* out_dev, void* stream);
 
+/* ---- Decode-step pieces around the matmuls (device pointers, stream-ordered).
+ * A Gemma-3 decode step is these plus the matmuls above (fused QKV, fused
+ * gate/up with the GeGLU epilogue, o, down, lm_head). The reference runs them
+ * on f32 host tensors; each entry cites the Rust code it replaces.
+ * The decode position is read from device memory (pos_dev) so a captured step
+ * can be replayed while qmm_add_int_dev advances it. */
+
+/* x[b] = scale * dequant(emb row tokens[b]) from a Q8_0 [vocab][hidden] tied
+ * embedding; token ids are clamped to [0, vocab). Replaces TokenEmbedding::
+ * forward + mul_scalar(embedding_scale) (model/main/src/core/forward.rs:122-127). */
+QMM_API int qmm_embed_q8_dev(const uint8_t* emb_dev, size_t vocab, size_t hidden, const int* tokens_dev,
+                             size_t batch, float scale, float* x_dev, void* stream);
+/* y = x / sqrt(mean(x^2) + eps) * (w + offset) per row. Replaces RMSNorm::
+ * forward (layers/main/src/core/rms_norm.rs:66-85, tensor math.rs:334-380). */
+QMM_API int qmm_rmsnorm_dev(const float* x_dev, const float* w_dev, float offset, float eps, size_t rows, size_t dim,
+                            float* y_dev, void* stream);
+/* x += rmsnorm(branch, w_post); then (w_next non-null) h = rmsnorm(x, w_next):
+ * a sandwich post-norm and residual add fused with the next pre-norm
+ * (layers/main/src/core/transformer_block.rs:424-449). */
+QMM_API int qmm_residual_rmsnorm_dev(float* x_dev, const float* branch_dev, const float* w_post_dev,
+                                     const float* w_next_dev, float offset, float eps, size_t rows, size_t dim,
+                                     float* h_dev, void* stream);
+/* From fused q|k|v rows [batch][(n_heads + 2 n_kv_heads) head_dim]: per-head
+ * RMSNorm of q and k, half-split RoPE with cos/sin tables [ctx][head_dim/2]
+ * at position *pos_dev; q into q_out [batch][n_heads][head_dim], k and v into
+ * the caches [batch][n_kv_heads][ctx][head_dim] at that position. head_dim a
+ * multiple of 64, at most 256 (layers/main/src/core/attention.rs:505-540,
+ * rope.rs:7-130). */
+QMM_API int qmm_qk_rope_cache_dev(const float* qkv_dev, size_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                  const float* q_norm_dev, const float* k_norm_dev, float offset, float eps,
+                                  const float* cos_dev, const float* sin_dev, const int* pos_dev, int ctx,
+                                  float* q_out_dev, float* k_cache_dev, float* v_cache_dev, void* stream);
+/* Floats of the partial-result buffer qmm_attention_decode_dev needs. */
+QMM_API size_t qmm_attention_partial_floats(size_t batch, int n_heads, int head_dim, int ctx);
+/* Single-token attention over cache positions 0..*pos_dev: scores q.k *
+ * inv_scale, softmax, weighted sum of v; grouped-query heads share their kv
+ * head. out [batch][n_heads * head_dim]. At most 8 heads and head_dim 256
+ * (layers/main/src/core/attention.rs:545-600, decode: no mask). */
+QMM_API int qmm_attention_decode_dev(const float* q_dev, const float* k_cache_dev, const float* v_cache_dev,
+                                     size_t batch, int n_heads, int n_kv_heads, int head_dim, const int* pos_dev,
+                                     int ctx, float inv_scale, float* partial_dev, float* out_dev, void* stream);
+/* *p_dev += value, stream-ordered (advances a captured step's position). */
+QMM_API int qmm_add_int_dev(int* p_dev, int value, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,7 @@ RELU = 2
 _P = ctypes.c_void_p
 _SZ = ctypes.c_size_t
 _I = ctypes.c_int
+_F = ctypes.c_float
 _HOST_MM = (_I, [_P, _SZ, _P, _SZ, _SZ, _SZ, _SZ, _P])
 SIGNATURES = {
     "qmm_version": (_I, []),
@@ -82,6 +83,14 @@ SIGNATURES = {
     "qmm_weight_fuse_gate_up": (_I, [_P, _P, _P]),
     "qmm_weight_gate_hidden": (_I, [_P, _P]),
     "qmm_gated_forward": (_I, [_P, _P, _SZ, _P, _I, _P]),
+    # decode-step pieces
+    "qmm_embed_q8_dev": (_I, [_P, _SZ, _SZ, _P, _SZ, _F, _P, _P]),
+    "qmm_rmsnorm_dev": (_I, [_P, _P, _F, _F, _SZ, _SZ, _P, _P]),
+    "qmm_residual_rmsnorm_dev": (_I, [_P, _P, _P, _P, _F, _F, _SZ, _SZ, _P, _P]),
+    "qmm_qk_rope_cache_dev": (_I, [_P, _SZ, _I, _I, _I, _P, _P, _F, _F, _P, _P, _P, _I, _P, _P, _P, _P]),
+    "qmm_attention_partial_floats": (_SZ, [_SZ, _I, _I, _I]),
+    "qmm_attention_decode_dev": (_I, [_P, _P, _P, _SZ, _I, _I, _I, _P, _I, _F, _P, _P, _P]),
+    "qmm_add_int_dev": (_I, [_P, _I, _P]),
 }
 
 

@@ -804,3 +804,78 @@ QMM_API int qmm_gated_act_dev(int act_fn, const float* gate_dev, const float* up
 }
 
 }  // extern "C"
+
+// ---- decode-step pieces (device pointers, stream-ordered) ------------------------
+namespace {
+bool dims_ok(size_t v) { return v > 0 && v <= (size_t)INT32_MAX; }
+}  // namespace
+
+QMM_API int qmm_embed_q8_dev(const uint8_t* emb_dev, size_t vocab, size_t hidden, const int* tokens_dev,
+                             size_t batch, float scale, float* x_dev, void* stream) {
+    if (!emb_dev || !tokens_dev || !x_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (hidden % QK) return fail(QMM_ERR_BLOCK_ALIGNMENT, "hidden size not divisible by 32");
+    if (!dims_ok(vocab) || !dims_ok(hidden) || batch > (size_t)INT32_MAX)
+        return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    cudaError_t e = launch_embed_q8(emb_dev, (int)hidden, tokens_dev, (int)batch, (int)vocab, scale, x_dev,
+                                    (cudaStream_t)stream);
+    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "embed");
+}
+
+QMM_API int qmm_rmsnorm_dev(const float* x_dev, const float* w_dev, float offset, float eps, size_t rows, size_t dim,
+                            float* y_dev, void* stream) {
+    if (!x_dev || !w_dev || !y_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (!dims_ok(dim) || rows > (size_t)INT32_MAX) return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    cudaError_t e = launch_rmsnorm(x_dev, w_dev, offset, eps, (int)rows, (int)dim, y_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "rmsnorm");
+}
+
+QMM_API int qmm_residual_rmsnorm_dev(float* x_dev, const float* branch_dev, const float* w_post_dev,
+                                     const float* w_next_dev, float offset, float eps, size_t rows, size_t dim,
+                                     float* h_dev, void* stream) {
+    if (!x_dev || !branch_dev || !w_post_dev || (w_next_dev && !h_dev))
+        return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (!dims_ok(dim) || rows > (size_t)INT32_MAX) return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    cudaError_t e = launch_residual_norm(x_dev, branch_dev, w_post_dev, w_next_dev, offset, eps, (int)rows, (int)dim,
+                                         h_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "residual rmsnorm");
+}
+
+QMM_API int qmm_qk_rope_cache_dev(const float* qkv_dev, size_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                  const float* q_norm_dev, const float* k_norm_dev, float offset, float eps,
+                                  const float* cos_dev, const float* sin_dev, const int* pos_dev, int ctx,
+                                  float* q_out_dev, float* k_cache_dev, float* v_cache_dev, void* stream) {
+    if (!qkv_dev || !q_norm_dev || !k_norm_dev || !cos_dev || !sin_dev || !pos_dev || !q_out_dev || !k_cache_dev ||
+        !v_cache_dev)
+        return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0 || head_dim % 64 ||
+        head_dim > 256 || ctx <= 0 || batch > (size_t)INT32_MAX)
+        return fail(QMM_ERR_SHAPE_MISMATCH, "heads, head_dim (a multiple of 64, at most 256) or context out of range");
+    cudaError_t e = launch_qk_rope_cache(qkv_dev, (int)batch, n_heads, n_kv_heads, head_dim, q_norm_dev, k_norm_dev,
+                                         offset, eps, cos_dev, sin_dev, pos_dev, ctx, q_out_dev, k_cache_dev,
+                                         v_cache_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "qk rope cache");
+}
+
+QMM_API size_t qmm_attention_partial_floats(size_t batch, int n_heads, int head_dim, int ctx) {
+    if (batch > (size_t)INT32_MAX || n_heads <= 0 || head_dim <= 0 || ctx <= 0) return 0;
+    return attn_partial_floats((int)batch, n_heads, head_dim, ctx);
+}
+
+QMM_API int qmm_attention_decode_dev(const float* q_dev, const float* k_cache_dev, const float* v_cache_dev,
+                                     size_t batch, int n_heads, int n_kv_heads, int head_dim, const int* pos_dev,
+                                     int ctx, float inv_scale, float* partial_dev, float* out_dev, void* stream) {
+    if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !partial_dev || !out_dev)
+        return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (n_heads <= 0 || n_heads > 8 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0 || head_dim > 256 ||
+        ctx <= 0 || batch > (size_t)INT32_MAX)
+        return fail(QMM_ERR_SHAPE_MISMATCH, "heads (at most 8), head_dim (at most 256) or context out of range");
+    cudaError_t e = launch_attention(q_dev, k_cache_dev, v_cache_dev, (int)batch, n_heads, n_kv_heads, head_dim,
+                                     pos_dev, ctx, inv_scale, partial_dev, out_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "attention");
+}
+
+QMM_API int qmm_add_int_dev(int* p_dev, int value, void* stream) {
+    if (!p_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    cudaError_t e = launch_add_int(p_dev, value, (cudaStream_t)stream);
+    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "add int");
+}

@@ -1,0 +1,324 @@
+// The non-matmul steps of a Gemma-3 decode step on the device (sm_100a): the
+// token embedding gather, the sandwich RMSNorms with their residual adds, the
+// per-head Q/K RMSNorm + rotary embedding + KV-cache append, and single-token
+// attention over the cache. The projections themselves are the library's
+// quantised matmuls (fused QKV, fused gate/up with the GeGLU epilogue, o,
+// down, lm_head).
+//
+// Reference (the per-layer order and arithmetic restated here):
+//   model forward_with_cache_pass  llmserve/llmmodel/model/main/src/core/forward.rs:107-239
+//   TransformerBlock (4 norms)     llmserve/llmmodel/layers/main/src/core/transformer_block.rs:371-449
+//   attention decode               llmserve/llmmodel/layers/main/src/core/attention.rs:454-610
+//   RMSNorm (weight + offset)      llmserve/llmmodel/layers/main/src/core/rms_norm.rs:71-85,
+//                                  main/features/tensor/src/core/tensor/math.rs:21-80 (rms = sqrt(mean(x^2) + eps))
+//   RoPE (half split, f32 tables)  llmserve/llmmodel/layers/main/src/core/rope.rs:7-130
+//
+// The decode position is read from device memory (pos_dev), so a whole step
+// can be captured once in a CUDA graph and replayed as the position advances.
+// The attention grid covers the cache's capacity; chunks past the position
+// write an empty partial.
+#include <cuda_fp16.h>
+
+#include "qmm_common.cuh"
+#include "qmm_kernels.cuh"
+
+namespace qmm {
+
+namespace {
+
+constexpr int kDecThreads = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Sum over the CTA (kDecThreads threads); every thread gets the total.
+__device__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();  // red is reused between calls
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kDecThreads / 32; ++w) t += red[w];
+    return t;
+}
+
+// x[b][i] = scale * d * q for token tokens[b]'s Q8_0 row (the tied embedding).
+__global__ void __launch_bounds__(kDecThreads) embed_q8_kernel(const uint8_t* __restrict__ emb, int hidden,
+                                                               const int* __restrict__ tokens, int vocab, float scale,
+                                                               float* __restrict__ x) {
+    const int b = blockIdx.x;
+    int tok = tokens[b];
+    tok = tok < 0 ? 0 : (tok >= vocab ? vocab - 1 : tok);
+    const uint8_t* row = emb + (size_t)tok * (hidden / QK) * 34;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        const uint8_t* blk = row + (i / QK) * 34;
+        const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+        const float q = (float)(int8_t)blk[2 + i % QK];
+        x[(size_t)b * hidden + i] = (d * q) * scale;
+    }
+}
+
+// y = x / sqrt(mean(x^2) + eps) * (w + offset), one CTA per row.
+__global__ void __launch_bounds__(kDecThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                              float offset, float eps, int dim, float* __restrict__ y) {
+    __shared__ float red[kDecThreads / 32];
+    const float* xr = x + (size_t)blockIdx.x * dim;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) y[(size_t)blockIdx.x * dim + i] = (xr[i] * inv) * (w[i] + offset);
+}
+
+// x += rmsnorm(branch) * (w_post + offset); then, if w_next, h = rmsnorm(x) *
+// (w_next + offset): a block's post-norm and residual add fused with the next
+// pre-norm.
+__global__ void __launch_bounds__(kDecThreads) residual_norm_kernel(float* __restrict__ x,
+                                                                    const float* __restrict__ branch,
+                                                                    const float* __restrict__ w_post,
+                                                                    const float* __restrict__ w_next, float offset,
+                                                                    float eps, int dim, float* __restrict__ h) {
+    __shared__ float red[kDecThreads / 32];
+    const size_t r0 = (size_t)blockIdx.x * dim;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += branch[r0 + i] * branch[r0 + i];
+    ss = block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+    float ss2 = 0.0f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float v = x[r0 + i] + (branch[r0 + i] * inv) * (w_post[i] + offset);
+        x[r0 + i] = v;
+        ss2 += v * v;
+    }
+    if (w_next == nullptr) return;
+    ss2 = block_sum(ss2, red);
+    const float inv2 = 1.0f / sqrtf(ss2 / (float)dim + eps);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) h[r0 + i] = (x[r0 + i] * inv2) * (w_next[i] + offset);
+}
+
+// One warp per head vector of one token: q heads get RMSNorm (q_norm) and
+// RoPE into q_out; the k head gets RMSNorm (k_norm) and RoPE, the v head is
+// copied, both into the cache at the current position. RoPE: first half
+// x1*cos - x2*sin, second half x1*sin + x2*cos, tables [ctx][hd/2].
+// hd <= 256, a multiple of 64.
+__global__ void __launch_bounds__(kDecThreads) qk_rope_cache_kernel(
+    const float* __restrict__ qkv, int nq, int nkv, int hd, const float* __restrict__ qn_w,
+    const float* __restrict__ kn_w, float offset, float eps, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, const int* __restrict__ pos_dev, int ctx, float* __restrict__ q_out,
+    float* __restrict__ k_cache, float* __restrict__ v_cache) {
+    const int b = blockIdx.x;
+    const int vec = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);  // 0..nq+2*nkv-1
+    const int lane = threadIdx.x & 31;
+    if (vec >= nq + 2 * nkv) return;
+    const int pos = *pos_dev;
+    if (pos < 0 || pos >= ctx) return;
+    const int row = nq + 2 * nkv;
+    const float* src = qkv + ((size_t)b * row + vec) * hd;
+    const int half = hd / 2, per = half / 32;  // pairs per lane (<= 4)
+    float x1[4], x2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (j < per) {
+            x1[j] = src[lane + 32 * j];
+            x2[j] = src[half + lane + 32 * j];
+        }
+    }
+    if (vec >= nq + nkv) {  // v: straight into the cache
+        float* dst = v_cache + (((size_t)b * nkv + (vec - nq - nkv)) * ctx + pos) * hd;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (j < per) {
+                dst[lane + 32 * j] = x1[j];
+                dst[half + lane + 32 * j] = x2[j];
+            }
+        }
+        return;
+    }
+    const float* nw = vec < nq ? qn_w : kn_w;
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        if (j < per) ss += x1[j] * x1[j] + x2[j] * x2[j];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+    const float* ct = cos_t + (size_t)pos * half;
+    const float* st = sin_t + (size_t)pos * half;
+    float* dst = vec < nq ? q_out + ((size_t)b * nq + vec) * hd
+                          : k_cache + (((size_t)b * nkv + (vec - nq)) * ctx + pos) * hd;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (j < per) {
+            const int i = lane + 32 * j;
+            const float a = (x1[j] * inv) * (nw[i] + offset);
+            const float c = (x2[j] * inv) * (nw[half + i] + offset);
+            dst[i] = a * ct[i] - c * st[i];
+            dst[half + i] = a * st[i] + c * ct[i];
+        }
+    }
+}
+
+// Partial attention over positions [c*kAttnChunk, ...] <= pos of one token b:
+// every q head of a kv head shares the chunk's K/V. Per head: m = max score,
+// l = sum exp(s - m), acc = sum exp(s - m) v. Scores = q.k * inv_scale.
+constexpr int kAttnChunk = 64;
+constexpr int kMaxHeads = 8;
+__global__ void __launch_bounds__(kDecThreads) attn_partial_kernel(
+    const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache, int nq,
+    int nkv, int hd, const int* __restrict__ pos_dev, int ctx, float inv_scale, float* __restrict__ part) {
+    __shared__ float qs[kMaxHeads * 256];
+    __shared__ float sc[kMaxHeads * kAttnChunk];
+    const int c = blockIdx.x, b = blockIdx.y;
+    const int nchunk = gridDim.x;
+    const int pos = *pos_dev;
+    const int t0 = c * kAttnChunk;
+    const int len = min(kAttnChunk, pos + 1 - t0);  // positions in this chunk (<= 0: none)
+    const int g = nq / nkv;                          // q heads per kv head
+    float* pbase = part + ((size_t)b * nchunk + c) * nq * (hd + 2);
+    if (len <= 0 || pos >= ctx) {
+        for (int h = threadIdx.x; h < nq; h += blockDim.x) {
+            pbase[h * (hd + 2) + hd] = -INFINITY;
+            pbase[h * (hd + 2) + hd + 1] = 0.0f;
+        }
+        return;
+    }
+    for (int i = threadIdx.x; i < nq * hd; i += blockDim.x) qs[i] = q[(size_t)b * nq * hd + i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int kv = 0; kv < nkv; ++kv) {
+        const float* kc = k_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd;
+        const float* vc = v_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd;
+        for (int t = warp; t < len; t += nw) {
+            float kr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) kr[j] = (lane + 32 * j < hd) ? kc[(size_t)t * hd + lane + 32 * j] : 0.0f;
+            for (int hh = 0; hh < g; ++hh) {
+                const int h = kv * g + hh;
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (lane + 32 * j < hd) s += qs[h * hd + lane + 32 * j] * kr[j];
+                s = warp_sum(s);
+                if (lane == 0) sc[h * kAttnChunk + t] = s * inv_scale;
+            }
+        }
+        __syncthreads();
+        for (int hh = 0; hh < g; ++hh) {
+            const int h = kv * g + hh;
+            float* e = sc + h * kAttnChunk;
+            float m = -INFINITY;
+            for (int t = 0; t < len; ++t) m = fmaxf(m, e[t]);
+            __syncthreads();  // every thread has read the scores
+            if ((int)threadIdx.x < len) e[threadIdx.x] = expf(e[threadIdx.x] - m);
+            __syncthreads();
+            for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+                float acc = 0.0f;
+                for (int t = 0; t < len; ++t) acc += e[t] * vc[(size_t)t * hd + d];
+                pbase[h * (hd + 2) + d] = acc;
+            }
+            if (threadIdx.x == 0) {
+                float l = 0.0f;
+                for (int t = 0; t < len; ++t) l += e[t];
+                pbase[h * (hd + 2) + hd] = m;
+                pbase[h * (hd + 2) + hd + 1] = l;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ctx[b][h*hd + d] = sum_c acc_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M).
+__global__ void __launch_bounds__(kDecThreads) attn_combine_kernel(const float* __restrict__ part, int nchunk, int nq,
+                                                                   int hd, float* __restrict__ out) {
+    const int b = blockIdx.x;
+    for (int h = 0; h < nq; ++h) {
+        float M = -INFINITY;
+        for (int c = 0; c < nchunk; ++c) M = fmaxf(M, part[(((size_t)b * nchunk + c) * nq + h) * (hd + 2) + hd]);
+        float L = 0.0f;
+        for (int c = 0; c < nchunk; ++c) {
+            const float* p = part + (((size_t)b * nchunk + c) * nq + h) * (hd + 2);
+            if (p[hd] != -INFINITY) L += p[hd + 1] * expf(p[hd] - M);
+        }
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+            float a = 0.0f;
+            for (int c = 0; c < nchunk; ++c) {
+                const float* p = part + (((size_t)b * nchunk + c) * nq + h) * (hd + 2);
+                if (p[hd] != -INFINITY) a += p[d] * expf(p[hd] - M);
+            }
+            out[((size_t)b * nq + h) * hd + d] = a / L;
+        }
+    }
+}
+
+__global__ void add_int_kernel(int* p, int v) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) *p += v;
+}
+
+}  // namespace
+
+cudaError_t launch_embed_q8(const uint8_t* emb, int hidden, const int* tokens, int batch, int vocab, float scale,
+                            float* x, cudaStream_t st) {
+    if (batch <= 0) return cudaSuccess;
+    embed_q8_kernel<<<batch, kDecThreads, 0, st>>>(emb, hidden, tokens, vocab, scale, x);
+    note_launch();
+    return cudaGetLastError();
+}
+cudaError_t launch_rmsnorm(const float* x, const float* w, float offset, float eps, int rows, int dim, float* y,
+                           cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    rmsnorm_kernel<<<rows, kDecThreads, 0, st>>>(x, w, offset, eps, dim, y);
+    note_launch();
+    return cudaGetLastError();
+}
+cudaError_t launch_residual_norm(float* x, const float* branch, const float* w_post, const float* w_next, float offset,
+                                 float eps, int rows, int dim, float* h, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    residual_norm_kernel<<<rows, kDecThreads, 0, st>>>(x, branch, w_post, w_next, offset, eps, dim, h);
+    note_launch();
+    return cudaGetLastError();
+}
+cudaError_t launch_qk_rope_cache(const float* qkv, int batch, int nq, int nkv, int hd, const float* qn_w,
+                                 const float* kn_w, float offset, float eps, const float* cos_t, const float* sin_t,
+                                 const int* pos_dev, int ctx, float* q_out, float* k_cache, float* v_cache,
+                                 cudaStream_t st) {
+    if (batch <= 0) return cudaSuccess;
+    if (hd % 64 || hd > 256) return cudaErrorInvalidValue;
+    const int vecs = nq + 2 * nkv, wpb = kDecThreads / 32;
+    qk_rope_cache_kernel<<<dim3(batch, (vecs + wpb - 1) / wpb), kDecThreads, 0, st>>>(
+        qkv, nq, nkv, hd, qn_w, kn_w, offset, eps, cos_t, sin_t, pos_dev, ctx, q_out, k_cache, v_cache);
+    note_launch();
+    return cudaGetLastError();
+}
+size_t attn_partial_floats(int batch, int nq, int hd, int ctx) {
+    return (size_t)batch * ((ctx + kAttnChunk - 1) / kAttnChunk) * nq * (hd + 2);
+}
+cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, int batch, int nq, int nkv,
+                             int hd, const int* pos_dev, int ctx, float inv_scale, float* part, float* out,
+                             cudaStream_t st) {
+    if (batch <= 0) return cudaSuccess;
+    if (nq > kMaxHeads || hd > 256 || nkv <= 0 || nq % nkv) return cudaErrorInvalidValue;
+    const int nchunk = (ctx + kAttnChunk - 1) / kAttnChunk;
+    attn_partial_kernel<<<dim3(nchunk, batch), kDecThreads, 0, st>>>(q, k_cache, v_cache, nq, nkv, hd, pos_dev, ctx,
+                                                                      inv_scale, part);
+    note_launch();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    attn_combine_kernel<<<batch, kDecThreads, 0, st>>>(part, nchunk, nq, hd, out);
+    note_launch();
+    return cudaGetLastError();
+}
+cudaError_t launch_add_int(int* p, int v, cudaStream_t st) {
+    add_int_kernel<<<1, 32, 0, st>>>(p, v);
+    note_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace qmm

@@ -35,6 +35,23 @@ cudaError_t launch_checksum(const uint8_t* p, uint64_t len, unsigned long long* 
 cudaError_t launch_gated_act(int kind, const float* gate, const float* up, int64_t m, int64_t hidden, int64_t ld,
                              float* out, cudaStream_t st);
 
+// ---- decode-step pieces around the matmuls (qmm_decode.cu) ----------------------
+cudaError_t launch_embed_q8(const uint8_t* emb, int hidden, const int* tokens, int batch, int vocab, float scale,
+                            float* x, cudaStream_t st);
+cudaError_t launch_rmsnorm(const float* x, const float* w, float offset, float eps, int rows, int dim, float* y,
+                           cudaStream_t st);
+cudaError_t launch_residual_norm(float* x, const float* branch, const float* w_post, const float* w_next, float offset,
+                                 float eps, int rows, int dim, float* h, cudaStream_t st);
+cudaError_t launch_qk_rope_cache(const float* qkv, int batch, int nq, int nkv, int hd, const float* qn_w,
+                                 const float* kn_w, float offset, float eps, const float* cos_t, const float* sin_t,
+                                 const int* pos_dev, int ctx, float* q_out, float* k_cache, float* v_cache,
+                                 cudaStream_t st);
+size_t attn_partial_floats(int batch, int nq, int hd, int ctx);
+cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, int batch, int nq, int nkv,
+                             int hd, const int* pos_dev, int ctx, float inv_scale, float* part, float* out,
+                             cudaStream_t st);
+cudaError_t launch_add_int(int* p, int v, cudaStream_t st);
+
 // ---- GEMV activation preparation (qmm_quant.cu) ----------------------------------
 // f32 mode:   xf [nb][M][4][16 halves];  native: xq [nb][M][4][8 bytes]
 // both:       side [nb][token_pad(M)/2][8 words] (see the kernels)

@@ -1,0 +1,94 @@
+"""Gemma-3 decode step on the GPU (machinelearning_b200/decode.py) against the
+oracle's restatement of the reference's forward pass with a KV cache
+(oracle/decode.py), on the same quantised block bytes: a small model of the
+Gemma-3 shape (6 layers so that layer 5 takes the global RoPE base, 4 query
+heads sharing 1 KV head, sandwich norms, GeGLU, tied Q8_0 embedding), several
+consecutive positions, batch 3. Logits within the 1e-3 contract."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+Q4_0, Q8_0 = 2, 8
+
+
+def small_config():
+    from machinelearning_b200.decode import Gemma3Config
+    return Gemma3Config(hidden=256, n_layers=6, n_heads=4, n_kv_heads=1, head_dim=64, ffn=512, vocab=640, ctx=16,
+                        emb_scale=float(np.float32(math.sqrt(256.0))))
+
+
+def host_weights(oracle, cfg, seed):
+    rng = np.random.default_rng(seed)
+    H, nq, nkv, hd = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    q4 = lambda n, k: oracle.quantize_q4_0(rng.normal(0, 0.05, n * k).astype(np.float32))  # noqa: E731
+    norm = lambda n: rng.normal(0, 0.1, n).astype(np.float32)  # noqa: E731
+    w = {"emb": oracle.quantize_q8_0(rng.normal(0, 0.05, cfg.vocab * H).astype(np.float32)),
+         "final_norm": norm(H), "layers": []}
+    for _ in range(cfg.n_layers):
+        w["layers"].append({
+            "qkv": q4((nq + 2 * nkv) * hd, H), "o": q4(H, nq * hd), "gate": q4(cfg.ffn, H), "up": q4(cfg.ffn, H),
+            "down": q4(H, cfg.ffn), "attn_norm": norm(H), "post_attn_norm": norm(H), "ffn_norm": norm(H),
+            "post_ffn_norm": norm(H), "q_norm": norm(hd), "k_norm": norm(hd)})
+    return w
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    assert torch.cuda.is_available()
+    return torch
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph):
+    from conftest import assert_close_rel
+    from oracle.decode import decode_step
+
+    from machinelearning_b200.decode import Gemma3Decoder
+    cfg = small_config()
+    w = host_weights(oracle, cfg, seed=11)
+    B = 3
+    model = Gemma3Decoder(cfg, w, batch=B)
+    kc = [np.zeros((B, cfg.n_kv_heads, cfg.ctx, cfg.head_dim), np.float32) for _ in range(cfg.n_layers)]
+    vc = [np.zeros_like(kc[0]) for _ in range(cfg.n_layers)]
+    rng = np.random.default_rng(12)
+    model.set_position(0)
+    if use_graph:
+        model.capture()
+    for pos in range(5):
+        tokens = rng.integers(0, cfg.vocab, B)
+        got = model.step(tokens).cpu().numpy()
+        ref = decode_step(cfg, w, tokens, pos, kc, vc)
+        assert_close_rel(got.ravel(), ref.ravel(), 1e-3)
+    assert int(model.pos.item()) == 5
+    model.close()
+
+
+def test_decode_cache_and_attention_pieces(oracle, torch_cuda):
+    """The cache after a step holds the reference's normed, rotated k and raw v
+    at the step's position (and nothing elsewhere)."""
+    from oracle.decode import decode_step
+
+    from machinelearning_b200.decode import Gemma3Decoder
+    cfg = small_config()
+    w = host_weights(oracle, cfg, seed=21)
+    B = 2
+    model = Gemma3Decoder(cfg, w, batch=B)
+    kc = [np.zeros((B, cfg.n_kv_heads, cfg.ctx, cfg.head_dim), np.float32) for _ in range(cfg.n_layers)]
+    vc = [np.zeros_like(kc[0]) for _ in range(cfg.n_layers)]
+    tokens = np.array([5, 600])
+    model.set_position(3)
+    model.step(tokens)
+    decode_step(cfg, w, tokens, 3, kc, vc)
+    k_dev = model.k_cache.cpu().numpy()
+    v_dev = model.v_cache.cpu().numpy()
+    for li in range(cfg.n_layers):
+        np.testing.assert_allclose(k_dev[li], kc[li], rtol=2e-3, atol=2e-4)
+        np.testing.assert_allclose(v_dev[li], vc[li], rtol=2e-3, atol=2e-4)
+    assert not k_dev[:, :, :, :3].any() and not k_dev[:, :, :, 4:].any()
+    model.close()

@@ -81,7 +81,10 @@ __global__ void __launch_bounds__(kDecThreads) rmsnorm_kernel(const float* __res
 
 // x += rmsnorm(branch) * (w_post + offset); then, if w_next, h = rmsnorm(x) *
 // (w_next + offset): a block's post-norm and residual add fused with the next
-// pre-norm.
+// pre-norm. Rows up to kNormRegs * kDecThreads wide are held in registers and
+// every input is loaded up front (one memory round trip, then the two
+// reductions); wider rows take the loop form.
+constexpr int kNormRegs = 8;
 __global__ void __launch_bounds__(kDecThreads) residual_norm_kernel(float* __restrict__ x,
                                                                     const float* __restrict__ branch,
                                                                     const float* __restrict__ w_post,
@@ -89,6 +92,40 @@ __global__ void __launch_bounds__(kDecThreads) residual_norm_kernel(float* __res
                                                                     float eps, int dim, float* __restrict__ h) {
     __shared__ float red[kDecThreads / 32];
     const size_t r0 = (size_t)blockIdx.x * dim;
+    if (dim <= kNormRegs * kDecThreads) {
+        float br[kNormRegs], xr[kNormRegs], wp[kNormRegs], wn[kNormRegs];
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) {
+            const int i = threadIdx.x + j * kDecThreads;
+            const bool in = i < dim;
+            br[j] = in ? branch[r0 + i] : 0.0f;
+            xr[j] = in ? x[r0 + i] : 0.0f;
+            wp[j] = in ? w_post[i] : 0.0f;
+            wn[j] = (in && w_next) ? w_next[i] : 0.0f;
+        }
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) ss += br[j] * br[j];
+        ss = block_sum(ss, red);
+        const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+        float ss2 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) {
+            const int i = threadIdx.x + j * kDecThreads;
+            xr[j] = xr[j] + (br[j] * inv) * (wp[j] + offset);
+            if (i < dim) x[r0 + i] = xr[j];
+            ss2 += i < dim ? xr[j] * xr[j] : 0.0f;
+        }
+        if (w_next == nullptr) return;
+        ss2 = block_sum(ss2, red);
+        const float inv2 = 1.0f / sqrtf(ss2 / (float)dim + eps);
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) {
+            const int i = threadIdx.x + j * kDecThreads;
+            if (i < dim) h[r0 + i] = (xr[j] * inv2) * (wn[j] + offset);
+        }
+        return;
+    }
     float ss = 0.0f;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += branch[r0 + i] * branch[r0 + i];
     ss = block_sum(ss, red);
@@ -166,16 +203,27 @@ __global__ void __launch_bounds__(kDecThreads) qk_rope_cache_kernel(
     }
 }
 
-// Partial attention over positions [c*kAttnChunk, ...] <= pos of one token b:
-// every q head of a kv head shares the chunk's K/V. Per head: m = max score,
-// l = sum exp(s - m), acc = sum exp(s - m) v. Scores = q.k * inv_scale.
-constexpr int kAttnChunk = 64;
+// Partial attention over positions [c*kAttnChunk, ...] <= pos of one token b.
+// The chunk's K and V rows are staged in shared memory with 16-byte loads
+// (all in flight together; K rows padded by one float so that threads reading
+// different rows at one column hit different banks), then: thread (h, t)
+// computes one score q_h . k_t * inv_scale; per head m = max, e_t = exp(s_t -
+// m), l = sum e_t; thread d accumulates acc_h[d] = sum_t e_t v_t[d] for every
+// head. q heads of one kv head share its rows.
+constexpr int kAttnChunk = 32;
 constexpr int kMaxHeads = 8;
+constexpr int kMaxHd = 256;
+__host__ __device__ constexpr size_t attn_smem_bytes(int hd) {
+    return (size_t)(kAttnChunk * (hd + 1) + kAttnChunk * hd + kMaxHeads * hd + kMaxHeads * kAttnChunk) * 4;
+}
 __global__ void __launch_bounds__(kDecThreads) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache, int nq,
     int nkv, int hd, const int* __restrict__ pos_dev, int ctx, float inv_scale, float* __restrict__ part) {
-    __shared__ float qs[kMaxHeads * 256];
-    __shared__ float sc[kMaxHeads * kAttnChunk];
+    extern __shared__ float asm_[];
+    float* ks = asm_;                           // [kAttnChunk][hd + 1]
+    float* vs = ks + kAttnChunk * (hd + 1);     // [kAttnChunk][hd]
+    float* qs = vs + kAttnChunk * hd;           // [nq][hd]
+    float* sc = qs + kMaxHeads * hd;            // [nq][kAttnChunk]
     const int c = blockIdx.x, b = blockIdx.y;
     const int nchunk = gridDim.x;
     const int pos = *pos_dev;
@@ -190,71 +238,77 @@ __global__ void __launch_bounds__(kDecThreads) attn_partial_kernel(
         }
         return;
     }
-    for (int i = threadIdx.x; i < nq * hd; i += blockDim.x) qs[i] = q[(size_t)b * nq * hd + i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int hd4 = hd / 4;
+    for (int i = threadIdx.x; i < nq * hd4; i += blockDim.x)
+        reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q + (size_t)b * nq * hd)[i];
     for (int kv = 0; kv < nkv; ++kv) {
-        const float* kc = k_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd;
-        const float* vc = v_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd;
-        for (int t = warp; t < len; t += nw) {
-            float kr[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) kr[j] = (lane + 32 * j < hd) ? kc[(size_t)t * hd + lane + 32 * j] : 0.0f;
-            for (int hh = 0; hh < g; ++hh) {
-                const int h = kv * g + hh;
-                float s = 0.0f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    if (lane + 32 * j < hd) s += qs[h * hd + lane + 32 * j] * kr[j];
-                s = warp_sum(s);
-                if (lane == 0) sc[h * kAttnChunk + t] = s * inv_scale;
-            }
+        const float4* kc = reinterpret_cast<const float4*>(k_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd);
+        const float4* vc = reinterpret_cast<const float4*>(v_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd);
+        __syncthreads();  // the previous kv head's rows are no longer read
+        for (int i = threadIdx.x; i < len * hd4; i += blockDim.x) {
+            const int t = i / hd4, j = i - t * hd4;
+            const float4 kv4 = kc[i], vv4 = vc[i];
+            float* kr = ks + t * (hd + 1) + 4 * j;
+            kr[0] = kv4.x;
+            kr[1] = kv4.y;
+            kr[2] = kv4.z;
+            kr[3] = kv4.w;
+            reinterpret_cast<float4*>(vs)[i] = vv4;
         }
         __syncthreads();
-        for (int hh = 0; hh < g; ++hh) {
-            const int h = kv * g + hh;
+        for (int i = threadIdx.x; i < g * len; i += blockDim.x) {
+            const int hh = i / len, t = i - hh * len;
+            const float* qh = qs + (kv * g + hh) * hd;
+            const float* kr = ks + t * (hd + 1);
+            float sacc = 0.0f;
+            for (int d = 0; d < hd; ++d) sacc += qh[d] * kr[d];
+            sc[(kv * g + hh) * kAttnChunk + t] = sacc * inv_scale;
+        }
+        __syncthreads();
+        if ((int)threadIdx.x < g) {  // per head: max, exponentials, their sum
+            const int h = kv * g + threadIdx.x;
             float* e = sc + h * kAttnChunk;
             float m = -INFINITY;
             for (int t = 0; t < len; ++t) m = fmaxf(m, e[t]);
-            __syncthreads();  // every thread has read the scores
-            if ((int)threadIdx.x < len) e[threadIdx.x] = expf(e[threadIdx.x] - m);
-            __syncthreads();
-            for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-                float acc = 0.0f;
-                for (int t = 0; t < len; ++t) acc += e[t] * vc[(size_t)t * hd + d];
-                pbase[h * (hd + 2) + d] = acc;
+            float l = 0.0f;
+            for (int t = 0; t < len; ++t) {
+                e[t] = expf(e[t] - m);
+                l += e[t];
             }
-            if (threadIdx.x == 0) {
-                float l = 0.0f;
-                for (int t = 0; t < len; ++t) l += e[t];
-                pbase[h * (hd + 2) + hd] = m;
-                pbase[h * (hd + 2) + hd + 1] = l;
-            }
+            pbase[h * (hd + 2) + hd] = m;
+            pbase[h * (hd + 2) + hd + 1] = l;
         }
         __syncthreads();
+        for (int i = threadIdx.x; i < g * hd; i += blockDim.x) {
+            const int hh = i / hd, d = i - hh * hd;
+            const float* e = sc + (kv * g + hh) * kAttnChunk;
+            float acc = 0.0f;
+            for (int t = 0; t < len; ++t) acc += e[t] * vs[t * hd + d];
+            pbase[(kv * g + hh) * (hd + 2) + d] = acc;
+        }
     }
 }
 
-// ctx[b][h*hd + d] = sum_c acc_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M).
+// out[b][h*hd + d] = sum_c acc_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M); one
+// thread per (head, d).
 __global__ void __launch_bounds__(kDecThreads) attn_combine_kernel(const float* __restrict__ part, int nchunk, int nq,
                                                                    int hd, float* __restrict__ out) {
     const int b = blockIdx.x;
-    for (int h = 0; h < nq; ++h) {
+    for (int i = threadIdx.x; i < nq * hd; i += blockDim.x) {
+        const int h = i / hd, d = i - h * hd;
+        const float* p0 = part + ((size_t)b * nchunk * nq + h) * (hd + 2);
+        const size_t cs = (size_t)nq * (hd + 2);  // chunk stride
         float M = -INFINITY;
-        for (int c = 0; c < nchunk; ++c) M = fmaxf(M, part[(((size_t)b * nchunk + c) * nq + h) * (hd + 2) + hd]);
-        float L = 0.0f;
+        for (int c = 0; c < nchunk; ++c) M = fmaxf(M, p0[c * cs + hd]);
+        float L = 0.0f, a = 0.0f;
         for (int c = 0; c < nchunk; ++c) {
-            const float* p = part + (((size_t)b * nchunk + c) * nq + h) * (hd + 2);
-            if (p[hd] != -INFINITY) L += p[hd + 1] * expf(p[hd] - M);
+            const float mc = p0[c * cs + hd];
+            if (mc == -INFINITY) continue;
+            const float f = expf(mc - M);
+            L += p0[c * cs + hd + 1] * f;
+            a += p0[c * cs + d] * f;
         }
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-            float a = 0.0f;
-            for (int c = 0; c < nchunk; ++c) {
-                const float* p = part + (((size_t)b * nchunk + c) * nq + h) * (hd + 2);
-                if (p[hd] != -INFINITY) a += p[d] * expf(p[hd] - M);
-            }
-            out[((size_t)b * nq + h) * hd + d] = a / L;
-        }
+        out[((size_t)b * nq + h) * hd + d] = a / L;
     }
 }
 
@@ -305,9 +359,13 @@ cudaError_t launch_attention(const float* q, const float* k_cache, const float* 
                              cudaStream_t st) {
     if (batch <= 0) return cudaSuccess;
     if (nq > kMaxHeads || hd > 256 || nkv <= 0 || nq % nkv) return cudaErrorInvalidValue;
+    if (hd % 4) return cudaErrorInvalidValue;
     const int nchunk = (ctx + kAttnChunk - 1) / kAttnChunk;
-    attn_partial_kernel<<<dim3(nchunk, batch), kDecThreads, 0, st>>>(q, k_cache, v_cache, nq, nkv, hd, pos_dev, ctx,
-                                                                      inv_scale, part);
+    const size_t smem = attn_smem_bytes(hd);
+    cudaError_t e0 = ensure_dynamic_smem((const void*)attn_partial_kernel, smem);
+    if (e0 != cudaSuccess) return e0;
+    attn_partial_kernel<<<dim3(nchunk, batch), kDecThreads, smem, st>>>(q, k_cache, v_cache, nq, nkv, hd, pos_dev,
+                                                                         ctx, inv_scale, part);
     note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;

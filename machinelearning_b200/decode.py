@@ -182,6 +182,10 @@ class Gemma3Decoder:
     def capture(self, advance: bool = True) -> None:
         """Record one step (and, with ``advance``, the position increment) as a
         CUDA graph; later ``step()`` calls replay it."""
+        # one direct launch first (it rewrites this position's cache rows with
+        # the same values): kernel attributes are set outside the capture
+        with torch.cuda.stream(self.stream):
+            self._launch(False)
         torch.cuda.synchronize(self.dev)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=self.stream):

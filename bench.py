@@ -625,7 +625,7 @@ def _decode_setup(args, local_rank, rank):
     cfg = Gemma3Config.gemma3_1b(ctx=512)
     w = random_weights(cfg, seed=1234 + rank, device=local_rank)
     model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank)
-    wbytes = model.emb.nbytes + sum(l[k].nbytes for l in model.layers for k in ("qkv", "o", "gate_up", "down"))
+    wbytes = model.lm_head.nbytes + sum(l[k].nbytes for l in model.layers for k in ("qkv", "o", "gate_up", "down"))
     return cfg, w, model, wbytes, torch
 
 

@@ -74,10 +74,29 @@ def rope_tables(head_dim: int, ctx: int, theta: float):
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
 
 
-def _quant_weight(dt: int, n: int, k: int, data, device: int) -> QuantWeight:
+def _quant_weight(dt: int, n: int, k: int, data, device: int, kpad: int = 0) -> QuantWeight:
+    """A library weight from block bytes; kpad > k: each row padded with
+    zero blocks (scale 0: every product 0) to kpad columns."""
+    bb = 34 if dt == Q8_0 else 18
+    if kpad > k:
+        t = data if isinstance(data, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(data, dtype=np.uint8))
+        t = t.to(torch.device("cuda", device))
+        padded = torch.zeros(n, (kpad // 32) * bb, dtype=torch.uint8, device=t.device)
+        padded[:, :(k // 32) * bb] = t.view(n, (k // 32) * bb)
+        return QuantWeight.from_device(dt, n, kpad, padded.reshape(-1))
     if isinstance(data, torch.Tensor):
         return QuantWeight.from_device(dt, n, k, data)
     return QuantWeight.from_host(dt, n, k, np.ascontiguousarray(data, dtype=np.uint8), device)
+
+
+def padded_k(k: int, batch: int) -> int:
+    """Columns a batch-matmul weight of k columns is padded to: batches of 17
+    or more run on the tensor-core GEMM, which needs a 16-byte row pitch (Q4_0
+    and Q8_0 rows are 18 and 34 bytes per 32 columns: a multiple of 8 blocks);
+    smaller batches keep k."""
+    if batch < 17 or (k // 32) % 8 == 0:
+        return k
+    return (k // 256 + 1) * 256
 
 
 class Gemma3Decoder:
@@ -97,14 +116,16 @@ class Gemma3Decoder:
                                    dtype=torch.float32).to(dev).contiguous()
 
         self.emb = _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device)
+        self.kh = kh = padded_k(H, batch)  # K of the matmuls that read the hidden state
+        self.lm_head = self.emb if kh == H else _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device, kh)
         self.final_norm = vec(weights["final_norm"])
         self.layers = []
         nqkv = (nq + 2 * nkv) * hd
         for lw in weights["layers"]:
-            gate = _quant_weight(Q4_0, cfg.ffn, H, lw["gate"], device)
-            up = _quant_weight(Q4_0, cfg.ffn, H, lw["up"], device)
+            gate = _quant_weight(Q4_0, cfg.ffn, H, lw["gate"], device, kh)
+            up = _quant_weight(Q4_0, cfg.ffn, H, lw["up"], device, kh)
             layer = {
-                "qkv": _quant_weight(Q4_0, nqkv, H, lw["qkv"], device),
+                "qkv": _quant_weight(Q4_0, nqkv, H, lw["qkv"], device, kh),
                 "o": _quant_weight(Q4_0, H, nq * hd, lw["o"], device),
                 "gate_up": fuse_gate_up(gate, up),
                 "down": _quant_weight(Q4_0, H, cfg.ffn, lw["down"], device),
@@ -123,6 +144,7 @@ class Gemma3Decoder:
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.x, self.h, self.o = z(B, H), z(B, H), z(B, H)
+        self.hp = self.h if kh == H else z(B, kh)  # h with a zero tail to kh columns
         self.qkv, self.q, self.attn = z(B, nqkv), z(B, nq * hd), z(B, nq * hd)
         self.ff = z(B, cfg.ffn)
         self.logits = z(B, cfg.vocab)
@@ -131,8 +153,8 @@ class Gemma3Decoder:
         self.stream = torch.cuda.Stream(dev)
         self.graph = None
         need = max(self.lib.qmm_workspace_size(dt, 0, B, n, k) for dt, n, k in
-                   [(Q4_0, nqkv, H), (Q4_0, H, nq * hd), (Q4_0, 2 * cfg.ffn, H), (Q4_0, H, cfg.ffn),
-                    (Q8_0, cfg.vocab, H)])
+                   [(Q4_0, nqkv, kh), (Q4_0, H, nq * hd), (Q4_0, 2 * cfg.ffn, kh), (Q4_0, H, cfg.ffn),
+                    (Q8_0, cfg.vocab, kh)])
         _lib.check(self.lib.qmm_reserve_workspace(device, ctypes.c_void_p(self.stream.cuda_stream), need + (1 << 20)))
 
     # ---- one step, issued on self.stream ---------------------------------------------
@@ -147,7 +169,8 @@ class Gemma3Decoder:
         for li, lw in enumerate(self.layers):
             theta = cfg.rope_global if (li + 1) % cfg.pattern == 0 else cfg.rope_local
             cos, sin = self.rope[theta]
-            ck(L.qmm_linear_forward(lw["qkv"].handle, P(self.h), B, P(self.qkv), 0, sp))
+            self._pad_h()
+            ck(L.qmm_linear_forward(lw["qkv"].handle, P(self.hp), B, P(self.qkv), 0, sp))
             ck(L.qmm_qk_rope_cache_dev(P(self.qkv), B, nq, nkv, hd, P(lw["q_norm"]), P(lw["k_norm"]), cfg.offset,
                                        cfg.eps, P(cos), P(sin), P(self.pos), cfg.ctx, P(self.q),
                                        P(self.k_cache[li]), P(self.v_cache[li]), sp))
@@ -156,14 +179,21 @@ class Gemma3Decoder:
             ck(L.qmm_linear_forward(lw["o"].handle, P(self.attn), B, P(self.o), 0, sp))
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_attn_norm"]), P(lw["ffn_norm"]),
                                           cfg.offset, cfg.eps, B, H, P(self.h), sp))
-            ck(L.qmm_gated_forward(lw["gate_up"].handle, P(self.h), B, P(self.ff), GELU, sp))
+            self._pad_h()
+            ck(L.qmm_gated_forward(lw["gate_up"].handle, P(self.hp), B, P(self.ff), GELU, sp))
             ck(L.qmm_linear_forward(lw["down"].handle, P(self.ff), B, P(self.o), 0, sp))
             nxt = self.layers[li + 1]["attn_norm"] if li + 1 < len(self.layers) else self.final_norm
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_ffn_norm"]), P(nxt), cfg.offset, cfg.eps,
                                           B, H, P(self.h), sp))
-        ck(L.qmm_linear_forward(self.emb.handle, P(self.h), B, P(self.logits), 0, sp))
+        self._pad_h()
+        ck(L.qmm_linear_forward(self.lm_head.handle, P(self.hp), B, P(self.logits), 0, sp))
         if advance:
             ck(L.qmm_add_int_dev(P(self.pos), 1, sp))
+
+    def _pad_h(self) -> None:
+        if self.hp is not self.h:
+            with torch.cuda.stream(self.stream):
+                self.hp[:, :self.cfg.hidden].copy_(self.h)
 
     def set_position(self, pos: int) -> None:
         if not 0 <= pos < self.cfg.ctx:
@@ -213,6 +243,8 @@ class Gemma3Decoder:
         for lw in self.layers:
             for key in ("qkv", "o", "gate_up", "down"):
                 lw[key].close()
+        if self.lm_head is not self.emb:
+            self.lm_head.close()
         self.emb.close()
 
 

@@ -16,10 +16,10 @@ pytestmark = pytest.mark.gpu
 Q4_0, Q8_0 = 2, 8
 
 
-def small_config():
+def small_config(hidden=256):
     from machinelearning_b200.decode import Gemma3Config
-    return Gemma3Config(hidden=256, n_layers=6, n_heads=4, n_kv_heads=1, head_dim=64, ffn=512, vocab=640, ctx=16,
-                        emb_scale=float(np.float32(math.sqrt(256.0))))
+    return Gemma3Config(hidden=hidden, n_layers=6, n_heads=4, n_kv_heads=1, head_dim=64, ffn=512, vocab=640, ctx=16,
+                        emb_scale=float(np.float32(math.sqrt(float(hidden)))))
 
 
 def host_weights(oracle, cfg, seed):
@@ -44,16 +44,18 @@ def torch_cuda():
     return torch
 
 
-@pytest.mark.parametrize("use_graph", [False, True])
-def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph):
+# (graph, batch, hidden): batch 20 with hidden 288 (9 blocks a row) runs the
+# hidden-state matmuls on the tensor-core GEMM over zero-padded 16-byte rows
+@pytest.mark.parametrize("use_graph,B,hidden", [(False, 3, 256), (True, 3, 256), (True, 20, 288)])
+def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph, B, hidden):
     from conftest import assert_close_rel
     from oracle.decode import decode_step
 
     from machinelearning_b200.decode import Gemma3Decoder
-    cfg = small_config()
+    cfg = small_config(hidden)
     w = host_weights(oracle, cfg, seed=11)
-    B = 3
     model = Gemma3Decoder(cfg, w, batch=B)
+    assert model.kh == (512 if B == 20 else hidden)
     kc = [np.zeros((B, cfg.n_kv_heads, cfg.ctx, cfg.head_dim), np.float32) for _ in range(cfg.n_layers)]
     vc = [np.zeros_like(kc[0]) for _ in range(cfg.n_layers)]
     rng = np.random.default_rng(12)
@@ -64,7 +66,10 @@ def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph):
         tokens = rng.integers(0, cfg.vocab, B)
         got = model.step(tokens).cpu().numpy()
         ref = decode_step(cfg, w, tokens, pos, kc, vc)
-        assert_close_rel(got.ravel(), ref.ravel(), 1e-3)
+        # norm-wise 1e-3 always; per element, the GEMM path (f16-rounded
+        # operands, outliers ~4e-3 of the rms per matmul) compounds over the
+        # layers, so its guard is 1e-2 of the rms
+        assert_close_rel(got.ravel(), ref.ravel(), 1e-3, 1e-2 if model.kh != hidden else None)
     assert int(model.pos.item()) == 5
     model.close()
 

@@ -156,8 +156,6 @@ __global__ void __launch_bounds__(kDecThreads) qk_rope_cache_kernel(
     const int vec = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);  // 0..nq+2*nkv-1
     const int lane = threadIdx.x & 31;
     if (vec >= nq + 2 * nkv) return;
-    const int pos = *pos_dev;
-    if (pos < 0 || pos >= ctx) return;
     const int row = nq + 2 * nkv;
     const float* src = qkv + ((size_t)b * row + vec) * hd;
     const int half = hd / 2, per = half / 32;  // pairs per lane (<= 4)
@@ -169,6 +167,8 @@ __global__ void __launch_bounds__(kDecThreads) qk_rope_cache_kernel(
             x2[j] = src[half + lane + 32 * j];
         }
     }
+    const int pos = *pos_dev;  // read after the row loads are in flight
+    if (pos < 0 || pos >= ctx) return;
     if (vec >= nq + nkv) {  // v: straight into the cache
         float* dst = v_cache + (((size_t)b * nkv + (vec - nq - nkv)) * ctx + pos) * hd;
 #pragma unroll
@@ -289,26 +289,44 @@ __global__ void __launch_bounds__(kDecThreads) attn_partial_kernel(
     }
 }
 
-// out[b][h*hd + d] = sum_c acc_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M); one
-// thread per (head, d).
+// out[b][h*hd + d] = sum_c acc_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M).
+// One CTA per (head, token): the chunks' (m, l) pairs are read once into
+// shared memory with their weights e^(m_c - M); thread d then sums its
+// column over the chunks (independent loads, unrolled).
+constexpr int kMaxChunks = 64;
 __global__ void __launch_bounds__(kDecThreads) attn_combine_kernel(const float* __restrict__ part, int nchunk, int nq,
                                                                    int hd, float* __restrict__ out) {
-    const int b = blockIdx.x;
-    for (int i = threadIdx.x; i < nq * hd; i += blockDim.x) {
-        const int h = i / hd, d = i - h * hd;
-        const float* p0 = part + ((size_t)b * nchunk * nq + h) * (hd + 2);
-        const size_t cs = (size_t)nq * (hd + 2);  // chunk stride
+    __shared__ float fw[kMaxChunks];
+    __shared__ float lw[kMaxChunks];
+    __shared__ float tot;
+    const int h = blockIdx.x, b = blockIdx.y;
+    const float* p0 = part + ((size_t)b * nchunk * nq + h) * (hd + 2);
+    const size_t cs = (size_t)nq * (hd + 2);  // chunk stride
+    if ((int)threadIdx.x < nchunk) {
+        fw[threadIdx.x] = p0[threadIdx.x * cs + hd];
+        lw[threadIdx.x] = p0[threadIdx.x * cs + hd + 1];
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
         float M = -INFINITY;
-        for (int c = 0; c < nchunk; ++c) M = fmaxf(M, p0[c * cs + hd]);
-        float L = 0.0f, a = 0.0f;
-        for (int c = 0; c < nchunk; ++c) {
-            const float mc = p0[c * cs + hd];
-            if (mc == -INFINITY) continue;
-            const float f = expf(mc - M);
-            L += p0[c * cs + hd + 1] * f;
-            a += p0[c * cs + d] * f;
+        for (int c = threadIdx.x; c < nchunk; c += 32) M = fmaxf(M, fw[c]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int c = threadIdx.x; c < nchunk; c += 32) {
+            const float f = fw[c] == -INFINITY ? 0.0f : expf(fw[c] - M);
+            fw[c] = f;
+            L += lw[c] * f;
         }
-        out[((size_t)b * nq + h) * hd + d] = a / L;
+        L = warp_sum(L);
+        if (threadIdx.x == 0) tot = L;
+    }
+    __syncthreads();
+    const float invL = 1.0f / tot;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float a = 0.0f;
+#pragma unroll 8
+        for (int c = 0; c < nchunk; ++c) a += fw[c] == 0.0f ? 0.0f : p0[c * cs + d] * fw[c];
+        out[((size_t)b * nq + h) * hd + d] = a * invL;
     }
 }
 
@@ -369,7 +387,8 @@ cudaError_t launch_attention(const float* q, const float* k_cache, const float* 
     note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    attn_combine_kernel<<<batch, kDecThreads, 0, st>>>(part, nchunk, nq, hd, out);
+    if (nchunk > kMaxChunks) return cudaErrorInvalidValue;
+    attn_combine_kernel<<<dim3(nq, batch), kDecThreads, 0, st>>>(part, nchunk, nq, hd, out);
     note_launch();
     return cudaGetLastError();
 }

@@ -277,6 +277,15 @@ QMM_API size_t qmm_attention_partial_floats(size_t batch, int n_heads, int head_
 QMM_API int qmm_attention_decode_dev(const float* q_dev, const float* k_cache_dev, const float* v_cache_dev,
                                      size_t batch, int n_heads, int n_kv_heads, int head_dim, const int* pos_dev,
                                      int ctx, float inv_scale, float* partial_dev, float* out_dev, void* stream);
+/* qmm_qk_rope_cache_dev and qmm_attention_decode_dev in one pass (one launch
+ * fewer per layer): every attention CTA normalises and rotates the q heads
+ * itself; the one holding the position writes k and v to the caches. Same
+ * arguments and limits (context at most 2048). */
+QMM_API int qmm_attention_decode_fused_dev(const float* qkv_dev, size_t batch, int n_heads, int n_kv_heads,
+                                           int head_dim, const float* q_norm_dev, const float* k_norm_dev, float offset,
+                                           float eps, const float* cos_dev, const float* sin_dev, const int* pos_dev,
+                                           int ctx, float* k_cache_dev, float* v_cache_dev, float inv_scale,
+                                           float* partial_dev, float* out_dev, void* stream);
 /* *p_dev += value, stream-ordered (advances a captured step's position). */
 QMM_API int qmm_add_int_dev(int* p_dev, int value, void* stream);
 

@@ -90,6 +90,8 @@ SIGNATURES = {
     "qmm_qk_rope_cache_dev": (_I, [_P, _SZ, _I, _I, _I, _P, _P, _F, _F, _P, _P, _P, _I, _P, _P, _P, _P]),
     "qmm_attention_partial_floats": (_SZ, [_SZ, _I, _I, _I]),
     "qmm_attention_decode_dev": (_I, [_P, _P, _P, _SZ, _I, _I, _I, _P, _I, _F, _P, _P, _P]),
+    "qmm_attention_decode_fused_dev": (_I, [_P, _SZ, _I, _I, _I, _P, _P, _F, _F, _P, _P, _P, _I, _P, _P, _F, _P, _P,
+                                            _P]),
     "qmm_add_int_dev": (_I, [_P, _I, _P]),
 }
 

@@ -874,6 +874,24 @@ QMM_API int qmm_attention_decode_dev(const float* q_dev, const float* k_cache_de
     return e == cudaSuccess ? QMM_OK : cuda_fail(e, "attention");
 }
 
+QMM_API int qmm_attention_decode_fused_dev(const float* qkv_dev, size_t batch, int n_heads, int n_kv_heads,
+                                           int head_dim, const float* q_norm_dev, const float* k_norm_dev, float offset,
+                                           float eps, const float* cos_dev, const float* sin_dev, const int* pos_dev,
+                                           int ctx, float* k_cache_dev, float* v_cache_dev, float inv_scale,
+                                           float* partial_dev, float* out_dev, void* stream) {
+    if (!qkv_dev || !q_norm_dev || !k_norm_dev || !cos_dev || !sin_dev || !pos_dev || !k_cache_dev || !v_cache_dev ||
+        !partial_dev || !out_dev)
+        return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (n_heads <= 0 || n_heads > 8 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0 || head_dim % 64 ||
+        head_dim > 256 || ctx <= 0 || ctx > 64 * 32 || batch > (size_t)INT32_MAX)
+        return fail(QMM_ERR_SHAPE_MISMATCH,
+                    "heads (at most 8), head_dim (a multiple of 64, at most 256) or context (at most 2048) out of range");
+    cudaError_t e = launch_attention_fused(qkv_dev, (int)batch, n_heads, n_kv_heads, head_dim, q_norm_dev, k_norm_dev,
+                                           offset, eps, cos_dev, sin_dev, pos_dev, ctx, k_cache_dev, v_cache_dev,
+                                           inv_scale, partial_dev, out_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "fused attention");
+}
+
 QMM_API int qmm_add_int_dev(int* p_dev, int value, void* stream) {
     if (!p_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
     cudaError_t e = launch_add_int(p_dev, value, (cudaStream_t)stream);

@@ -289,6 +289,151 @@ __global__ void __launch_bounds__(kDecThreads) attn_partial_kernel(
     }
 }
 
+// One head vector (hd values, one warp): rot -- RMSNorm with weight nw and
+// half-split RoPE with the position's cos/sin rows; else a copy. Written to
+// dst_a and, if non-null, dst_b (both contiguous over the vector).
+__device__ __forceinline__ void norm_rope_vec(const float* __restrict__ src, const float* __restrict__ nw, bool rot,
+                                              float offset, float eps, int hd, const float* __restrict__ ct,
+                                              const float* __restrict__ st, int lane, float* dst_a, float* dst_b) {
+    const int half = hd / 2, per = half / 32;
+    float x1[4], x2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (j < per) {
+            x1[j] = src[lane + 32 * j];
+            x2[j] = src[half + lane + 32 * j];
+        }
+    }
+    float inv = 1.0f;
+    if (rot) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (j < per) ss += x1[j] * x1[j] + x2[j] * x2[j];
+        ss = warp_sum(ss);
+        inv = 1.0f / sqrtf(ss / (float)hd + eps);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (j < per) {
+            const int i = lane + 32 * j;
+            float r1 = x1[j], r2 = x2[j];
+            if (rot) {
+                const float a = (x1[j] * inv) * (nw[i] + offset);
+                const float c = (x2[j] * inv) * (nw[half + i] + offset);
+                r1 = a * ct[i] - c * st[i];
+                r2 = a * st[i] + c * ct[i];
+            }
+            dst_a[i] = r1;
+            dst_a[half + i] = r2;
+            if (dst_b) {
+                dst_b[i] = r1;
+                dst_b[half + i] = r2;
+            }
+        }
+    }
+}
+
+// attn_partial_kernel with the QK-norm / RoPE / cache append folded in, from
+// the fused q|k|v rows: every CTA normalises and rotates its q heads itself
+// into shared memory; the CTA whose chunk holds the position also normalises
+// and rotates k and writes k and v to the cache and to its staged rows. No
+// other CTA reads that cache row. One launch fewer per layer.
+__global__ void __launch_bounds__(kDecThreads) attn_fused_kernel(
+    const float* __restrict__ qkv, int nq, int nkv, int hd, const float* __restrict__ qn_w,
+    const float* __restrict__ kn_w, float offset, float eps, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, const int* __restrict__ pos_dev, int ctx, float* __restrict__ k_cache,
+    float* __restrict__ v_cache, float inv_scale, float* __restrict__ part) {
+    extern __shared__ float asm_[];
+    float* ks = asm_;                           // [kAttnChunk][hd + 1]
+    float* vs = ks + kAttnChunk * (hd + 1);     // [kAttnChunk][hd]
+    float* qs = vs + kAttnChunk * hd;           // [nq][hd]
+    float* sc = qs + kMaxHeads * hd;            // [nq][kAttnChunk]
+    const int c = blockIdx.x, b = blockIdx.y;
+    const int nchunk = gridDim.x;
+    const int pos = *pos_dev;
+    const int t0 = c * kAttnChunk;
+    const int len = min(kAttnChunk, pos + 1 - t0);  // positions in this chunk (<= 0: none)
+    const int g = nq / nkv;                          // q heads per kv head
+    float* pbase = part + ((size_t)b * nchunk + c) * nq * (hd + 2);
+    if (len <= 0 || pos >= ctx) {
+        for (int h = threadIdx.x; h < nq; h += blockDim.x) {
+            pbase[h * (hd + 2) + hd] = -INFINITY;
+            pbase[h * (hd + 2) + hd + 1] = 0.0f;
+        }
+        return;
+    }
+    const int hd4 = hd / 4;
+    const bool owner = pos < t0 + kAttnChunk;  // this chunk holds the position
+    const int tp = pos - t0;                    // its row (owner only)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const float* src = qkv + (size_t)b * (nq + 2 * nkv) * hd;
+    const float* ct = cos_t + (size_t)pos * (hd / 2);
+    const float* st = sin_t + (size_t)pos * (hd / 2);
+    for (int kv = 0; kv < nkv; ++kv) {
+        const float4* kc = reinterpret_cast<const float4*>(k_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd);
+        const float4* vc = reinterpret_cast<const float4*>(v_cache + (((size_t)b * nkv + kv) * ctx + t0) * hd);
+        __syncthreads();  // the previous kv head's rows are no longer read
+        // this kv head's q heads (every CTA); its k and v at the position (the
+        // owner: into the cache and into the staged row)
+        const int nvec = g + (owner ? 2 : 0);
+        for (int v = warp; v < nvec; v += nw) {
+            if (v < g) {
+                const int h = kv * g + v;
+                norm_rope_vec(src + (size_t)h * hd, qn_w, true, offset, eps, hd, ct, st, lane, qs + h * hd, nullptr);
+            } else if (v == g) {
+                norm_rope_vec(src + (size_t)(nq + kv) * hd, kn_w, true, offset, eps, hd, ct, st, lane,
+                              k_cache + (((size_t)b * nkv + kv) * ctx + pos) * hd, ks + tp * (hd + 1));
+            } else {
+                norm_rope_vec(src + (size_t)(nq + nkv + kv) * hd, nullptr, false, offset, eps, hd, ct, st, lane,
+                              v_cache + (((size_t)b * nkv + kv) * ctx + pos) * hd, vs + tp * hd);
+            }
+        }
+        for (int i = threadIdx.x; i < len * hd4; i += blockDim.x) {
+            const int t = i / hd4, j = i - t * hd4;
+            if (owner && t == tp) continue;  // written above
+            const float4 kv4 = kc[i], vv4 = vc[i];
+            float* kr = ks + t * (hd + 1) + 4 * j;
+            kr[0] = kv4.x;
+            kr[1] = kv4.y;
+            kr[2] = kv4.z;
+            kr[3] = kv4.w;
+            reinterpret_cast<float4*>(vs)[i] = vv4;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < g * len; i += blockDim.x) {
+            const int hh = i / len, t = i - hh * len;
+            const float* qh = qs + (kv * g + hh) * hd;
+            const float* kr = ks + t * (hd + 1);
+            float sacc = 0.0f;
+            for (int d = 0; d < hd; ++d) sacc += qh[d] * kr[d];
+            sc[(kv * g + hh) * kAttnChunk + t] = sacc * inv_scale;
+        }
+        __syncthreads();
+        if ((int)threadIdx.x < g) {  // per head: max, exponentials, their sum
+            const int h = kv * g + threadIdx.x;
+            float* e = sc + h * kAttnChunk;
+            float m = -INFINITY;
+            for (int t = 0; t < len; ++t) m = fmaxf(m, e[t]);
+            float l = 0.0f;
+            for (int t = 0; t < len; ++t) {
+                e[t] = expf(e[t] - m);
+                l += e[t];
+            }
+            pbase[h * (hd + 2) + hd] = m;
+            pbase[h * (hd + 2) + hd + 1] = l;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < g * hd; i += blockDim.x) {
+            const int hh = i / hd, d = i - hh * hd;
+            const float* e = sc + (kv * g + hh) * kAttnChunk;
+            float acc = 0.0f;
+            for (int t = 0; t < len; ++t) acc += e[t] * vs[t * hd + d];
+            pbase[(kv * g + hh) * (hd + 2) + d] = acc;
+        }
+    }
+}
+
 // out[b][h*hd + d] = sum_c acc_c[d] e^(m_c - M) / sum_c l_c e^(m_c - M).
 // One CTA per (head, token): the chunks' (m, l) pairs are read once into
 // shared memory with their weights e^(m_c - M); thread d then sums its
@@ -388,6 +533,27 @@ cudaError_t launch_attention(const float* q, const float* k_cache, const float* 
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (nchunk > kMaxChunks) return cudaErrorInvalidValue;
+    attn_combine_kernel<<<dim3(nq, batch), kDecThreads, 0, st>>>(part, nchunk, nq, hd, out);
+    note_launch();
+    return cudaGetLastError();
+}
+cudaError_t launch_attention_fused(const float* qkv, int batch, int nq, int nkv, int hd, const float* qn_w,
+                                   const float* kn_w, float offset, float eps, const float* cos_t, const float* sin_t,
+                                   const int* pos_dev, int ctx, float* k_cache, float* v_cache, float inv_scale,
+                                   float* part, float* out, cudaStream_t st) {
+    if (batch <= 0) return cudaSuccess;
+    if (nq > kMaxHeads || hd > 256 || hd % 64 || nkv <= 0 || nq % nkv) return cudaErrorInvalidValue;
+    const int nchunk = (ctx + kAttnChunk - 1) / kAttnChunk;
+    if (nchunk > kMaxChunks) return cudaErrorInvalidValue;
+    const size_t smem = attn_smem_bytes(hd);
+    cudaError_t e = ensure_dynamic_smem((const void*)attn_fused_kernel, smem);
+    if (e != cudaSuccess) return e;
+    attn_fused_kernel<<<dim3(nchunk, batch), kDecThreads, smem, st>>>(qkv, nq, nkv, hd, qn_w, kn_w, offset, eps, cos_t,
+                                                                       sin_t, pos_dev, ctx, k_cache, v_cache,
+                                                                       inv_scale, part);
+    note_launch();
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
     attn_combine_kernel<<<dim3(nq, batch), kDecThreads, 0, st>>>(part, nchunk, nq, hd, out);
     note_launch();
     return cudaGetLastError();

@@ -50,6 +50,10 @@ size_t attn_partial_floats(int batch, int nq, int hd, int ctx);
 cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, int batch, int nq, int nkv,
                              int hd, const int* pos_dev, int ctx, float inv_scale, float* part, float* out,
                              cudaStream_t st);
+cudaError_t launch_attention_fused(const float* qkv, int batch, int nq, int nkv, int hd, const float* qn_w,
+                                   const float* kn_w, float offset, float eps, const float* cos_t, const float* sin_t,
+                                   const int* pos_dev, int ctx, float* k_cache, float* v_cache, float inv_scale,
+                                   float* part, float* out, cudaStream_t st);
 cudaError_t launch_add_int(int* p, int v, cudaStream_t st);
 
 // ---- GEMV activation preparation (qmm_quant.cu) ----------------------------------

@@ -104,8 +104,9 @@ class Gemma3Decoder:
     ``final_norm``, per layer ``qkv``/``o``/``gate``/``up``/``down`` Q4_0 bytes
     and the six norm vectors), as host numpy arrays or CUDA uint8 tensors."""
 
-    def __init__(self, cfg: Gemma3Config, weights: dict, batch: int, device: int = 0):
+    def __init__(self, cfg: Gemma3Config, weights: dict, batch: int, device: int = 0, fused_attention: bool = True):
         self.cfg, self.batch, self.device = cfg, batch, device
+        self.fused_attention = fused_attention  # QK-norm/RoPE/cache append inside the attention kernel
         dev = torch.device("cuda", device)
         self.dev = dev
         H, nq, nkv, hd = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
@@ -171,11 +172,17 @@ class Gemma3Decoder:
             cos, sin = self.rope[theta]
             self._pad_h()
             ck(L.qmm_linear_forward(lw["qkv"].handle, P(self.hp), B, P(self.qkv), 0, sp))
-            ck(L.qmm_qk_rope_cache_dev(P(self.qkv), B, nq, nkv, hd, P(lw["q_norm"]), P(lw["k_norm"]), cfg.offset,
-                                       cfg.eps, P(cos), P(sin), P(self.pos), cfg.ctx, P(self.q),
-                                       P(self.k_cache[li]), P(self.v_cache[li]), sp))
-            ck(L.qmm_attention_decode_dev(P(self.q), P(self.k_cache[li]), P(self.v_cache[li]), B, nq, nkv, hd,
-                                          P(self.pos), cfg.ctx, self.inv_scale, P(self.part), P(self.attn), sp))
+            if self.fused_attention:
+                ck(L.qmm_attention_decode_fused_dev(P(self.qkv), B, nq, nkv, hd, P(lw["q_norm"]), P(lw["k_norm"]),
+                                                    cfg.offset, cfg.eps, P(cos), P(sin), P(self.pos), cfg.ctx,
+                                                    P(self.k_cache[li]), P(self.v_cache[li]), self.inv_scale,
+                                                    P(self.part), P(self.attn), sp))
+            else:
+                ck(L.qmm_qk_rope_cache_dev(P(self.qkv), B, nq, nkv, hd, P(lw["q_norm"]), P(lw["k_norm"]), cfg.offset,
+                                           cfg.eps, P(cos), P(sin), P(self.pos), cfg.ctx, P(self.q),
+                                           P(self.k_cache[li]), P(self.v_cache[li]), sp))
+                ck(L.qmm_attention_decode_dev(P(self.q), P(self.k_cache[li]), P(self.v_cache[li]), B, nq, nkv, hd,
+                                              P(self.pos), cfg.ctx, self.inv_scale, P(self.part), P(self.attn), sp))
             ck(L.qmm_linear_forward(lw["o"].handle, P(self.attn), B, P(self.o), 0, sp))
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_attn_norm"]), P(lw["ffn_norm"]),
                                           cfg.offset, cfg.eps, B, H, P(self.h), sp))

@@ -46,15 +46,19 @@ def torch_cuda():
 
 # (graph, batch, hidden): batch 20 with hidden 288 (9 blocks a row) runs the
 # hidden-state matmuls on the tensor-core GEMM over zero-padded 16-byte rows
-@pytest.mark.parametrize("use_graph,B,hidden", [(False, 3, 256), (True, 3, 256), (True, 20, 288)])
-def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph, B, hidden):
+# fused: QK-norm / RoPE / cache append inside the attention kernel, or the
+# separate kernels (both C-ABI forms)
+@pytest.mark.parametrize("use_graph,B,hidden,fused", [(False, 3, 256, True), (True, 3, 256, True),
+                                                      (True, 20, 288, True), (False, 3, 256, False),
+                                                      (True, 20, 288, False)])
+def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph, B, hidden, fused):
     from conftest import assert_close_rel
     from oracle.decode import decode_step
 
     from machinelearning_b200.decode import Gemma3Decoder
     cfg = small_config(hidden)
     w = host_weights(oracle, cfg, seed=11)
-    model = Gemma3Decoder(cfg, w, batch=B)
+    model = Gemma3Decoder(cfg, w, batch=B, fused_attention=fused)
     assert model.kh == (512 if B == 20 else hidden)
     kc = [np.zeros((B, cfg.n_kv_heads, cfg.ctx, cfg.head_dim), np.float32) for _ in range(cfg.n_layers)]
     vc = [np.zeros_like(kc[0]) for _ in range(cfg.n_layers)]

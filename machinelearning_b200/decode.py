@@ -118,7 +118,10 @@ class Gemma3Decoder:
 
         self.emb = _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device)
         self.kh = kh = padded_k(H, batch)  # K of the matmuls that read the hidden state
-        self.lm_head = self.emb if kh == H else _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device, kh)
+        # the lm_head also at batch 1: a 16-byte row pitch lets its one-token
+        # matmul stream through the band kernel
+        self.klm = klm = kh if batch != 1 else padded_k(H, 17)
+        self.lm_head = self.emb if klm == H else _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device, klm)
         self.final_norm = vec(weights["final_norm"])
         self.layers = []
         nqkv = (nq + 2 * nkv) * hd
@@ -146,6 +149,7 @@ class Gemma3Decoder:
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.x, self.h, self.o = z(B, H), z(B, H), z(B, H)
         self.hp = self.h if kh == H else z(B, kh)  # h with a zero tail to kh columns
+        self.hl = self.hp if klm == kh else z(B, klm)  # the same for the lm_head
         self.qkv, self.q, self.attn = z(B, nqkv), z(B, nq * hd), z(B, nq * hd)
         self.ff = z(B, cfg.ffn)
         self.logits = z(B, cfg.vocab)
@@ -155,7 +159,7 @@ class Gemma3Decoder:
         self.graph = None
         need = max(self.lib.qmm_workspace_size(dt, 0, B, n, k) for dt, n, k in
                    [(Q4_0, nqkv, kh), (Q4_0, H, nq * hd), (Q4_0, 2 * cfg.ffn, kh), (Q4_0, H, cfg.ffn),
-                    (Q8_0, cfg.vocab, kh)])
+                    (Q8_0, cfg.vocab, klm)])
         _lib.check(self.lib.qmm_reserve_workspace(device, ctypes.c_void_p(self.stream.cuda_stream), need + (1 << 20)))
 
     # ---- one step, issued on self.stream ---------------------------------------------
@@ -193,7 +197,10 @@ class Gemma3Decoder:
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_ffn_norm"]), P(nxt), cfg.offset, cfg.eps,
                                           B, H, P(self.h), sp))
         self._pad_h()
-        ck(L.qmm_linear_forward(self.lm_head.handle, P(self.hp), B, P(self.logits), 0, sp))
+        if self.hl is not self.hp:
+            with torch.cuda.stream(self.stream):
+                self.hl[:, :H].copy_(self.h)
+        ck(L.qmm_linear_forward(self.lm_head.handle, P(self.hl), B, P(self.logits), 0, sp))
         if advance:
             ck(L.qmm_add_int_dev(P(self.pos), 1, sp))
 

@@ -50,7 +50,7 @@ def torch_cuda():
 # separate kernels (both C-ABI forms)
 @pytest.mark.parametrize("use_graph,B,hidden,fused", [(False, 3, 256, True), (True, 3, 256, True),
                                                       (True, 20, 288, True), (False, 3, 256, False),
-                                                      (True, 20, 288, False)])
+                                                      (True, 20, 288, False), (True, 1, 288, True)])
 def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph, B, hidden, fused):
     from conftest import assert_close_rel
     from oracle.decode import decode_step
@@ -60,6 +60,7 @@ def test_decode_steps_match_oracle(oracle, torch_cuda, use_graph, B, hidden, fus
     w = host_weights(oracle, cfg, seed=11)
     model = Gemma3Decoder(cfg, w, batch=B, fused_attention=fused)
     assert model.kh == (512 if B == 20 else hidden)
+    assert model.klm == (512 if hidden == 288 and B in (1, 20) else hidden)  # batch 1: padded lm_head only
     kc = [np.zeros((B, cfg.n_kv_heads, cfg.ctx, cfg.head_dim), np.float32) for _ in range(cfg.n_layers)]
     vc = [np.zeros_like(kc[0]) for _ in range(cfg.n_layers)]
     rng = np.random.default_rng(12)

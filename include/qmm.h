@@ -248,16 +248,17 @@ QMM_API int qmm_gated_act_dev(int act_fn, const float* gate_dev, const float* up
  * forward + mul_scalar(embedding_scale) (model/main/src/core/forward.rs:122-127). */
 QMM_API int qmm_embed_q8_dev(const uint8_t* emb_dev, size_t vocab, size_t hidden, const int* tokens_dev,
                              size_t batch, float scale, float* x_dev, void* stream);
-/* y = x / sqrt(mean(x^2) + eps) * (w + offset) per row. Replaces RMSNorm::
- * forward (layers/main/src/core/rms_norm.rs:66-85, tensor math.rs:334-380). */
+/* y = x / sqrt(mean(x^2) + eps) * (w + offset) per row; y rows ld_y floats
+ * apart (0: dim; wider rows keep their tail). Replaces RMSNorm::forward
+ * (layers/main/src/core/rms_norm.rs:66-85, tensor math.rs:334-380). */
 QMM_API int qmm_rmsnorm_dev(const float* x_dev, const float* w_dev, float offset, float eps, size_t rows, size_t dim,
-                            float* y_dev, void* stream);
-/* x += rmsnorm(branch, w_post); then (w_next non-null) h = rmsnorm(x, w_next):
- * a sandwich post-norm and residual add fused with the next pre-norm
- * (layers/main/src/core/transformer_block.rs:424-449). */
+                            float* y_dev, size_t ld_y, void* stream);
+/* x += rmsnorm(branch, w_post); then (w_next non-null) h = rmsnorm(x, w_next),
+ * h rows ld_h floats apart (0: dim): a sandwich post-norm and residual add
+ * fused with the next pre-norm (layers/main/src/core/transformer_block.rs:424-449). */
 QMM_API int qmm_residual_rmsnorm_dev(float* x_dev, const float* branch_dev, const float* w_post_dev,
                                      const float* w_next_dev, float offset, float eps, size_t rows, size_t dim,
-                                     float* h_dev, void* stream);
+                                     float* h_dev, size_t ld_h, void* stream);
 /* From fused q|k|v rows [batch][(n_heads + 2 n_kv_heads) head_dim]: per-head
  * RMSNorm of q and k, half-split RoPE with cos/sin tables [ctx][head_dim/2]
  * at position *pos_dev; q into q_out [batch][n_heads][head_dim], k and v into

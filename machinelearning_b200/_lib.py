@@ -85,8 +85,8 @@ SIGNATURES = {
     "qmm_gated_forward": (_I, [_P, _P, _SZ, _P, _I, _P]),
     # decode-step pieces
     "qmm_embed_q8_dev": (_I, [_P, _SZ, _SZ, _P, _SZ, _F, _P, _P]),
-    "qmm_rmsnorm_dev": (_I, [_P, _P, _F, _F, _SZ, _SZ, _P, _P]),
-    "qmm_residual_rmsnorm_dev": (_I, [_P, _P, _P, _P, _F, _F, _SZ, _SZ, _P, _P]),
+    "qmm_rmsnorm_dev": (_I, [_P, _P, _F, _F, _SZ, _SZ, _P, _SZ, _P]),
+    "qmm_residual_rmsnorm_dev": (_I, [_P, _P, _P, _P, _F, _F, _SZ, _SZ, _P, _SZ, _P]),
     "qmm_qk_rope_cache_dev": (_I, [_P, _SZ, _I, _I, _I, _P, _P, _F, _F, _P, _P, _P, _I, _P, _P, _P, _P]),
     "qmm_attention_partial_floats": (_SZ, [_SZ, _I, _I, _I]),
     "qmm_attention_decode_dev": (_I, [_P, _P, _P, _SZ, _I, _I, _I, _P, _I, _F, _P, _P, _P]),

@@ -822,21 +822,24 @@ QMM_API int qmm_embed_q8_dev(const uint8_t* emb_dev, size_t vocab, size_t hidden
 }
 
 QMM_API int qmm_rmsnorm_dev(const float* x_dev, const float* w_dev, float offset, float eps, size_t rows, size_t dim,
-                            float* y_dev, void* stream) {
+                            float* y_dev, size_t ld_y, void* stream) {
     if (!x_dev || !w_dev || !y_dev) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
-    if (!dims_ok(dim) || rows > (size_t)INT32_MAX) return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
-    cudaError_t e = launch_rmsnorm(x_dev, w_dev, offset, eps, (int)rows, (int)dim, y_dev, (cudaStream_t)stream);
+    if (!dims_ok(dim) || rows > (size_t)INT32_MAX || ld_y > (size_t)INT32_MAX || (ld_y && ld_y < dim))
+        return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    cudaError_t e = launch_rmsnorm(x_dev, w_dev, offset, eps, (int)rows, (int)dim, y_dev, (int)ld_y,
+                                   (cudaStream_t)stream);
     return e == cudaSuccess ? QMM_OK : cuda_fail(e, "rmsnorm");
 }
 
 QMM_API int qmm_residual_rmsnorm_dev(float* x_dev, const float* branch_dev, const float* w_post_dev,
                                      const float* w_next_dev, float offset, float eps, size_t rows, size_t dim,
-                                     float* h_dev, void* stream) {
+                                     float* h_dev, size_t ld_h, void* stream) {
     if (!x_dev || !branch_dev || !w_post_dev || (w_next_dev && !h_dev))
         return fail(QMM_ERR_INVALID_INPUT, "null pointer");
-    if (!dims_ok(dim) || rows > (size_t)INT32_MAX) return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
+    if (!dims_ok(dim) || rows > (size_t)INT32_MAX || ld_h > (size_t)INT32_MAX || (ld_h && ld_h < dim))
+        return fail(QMM_ERR_SHAPE_MISMATCH, "shape out of range");
     cudaError_t e = launch_residual_norm(x_dev, branch_dev, w_post_dev, w_next_dev, offset, eps, (int)rows, (int)dim,
-                                         h_dev, (cudaStream_t)stream);
+                                         h_dev, (int)ld_h, (cudaStream_t)stream);
     return e == cudaSuccess ? QMM_OK : cuda_fail(e, "residual rmsnorm");
 }
 

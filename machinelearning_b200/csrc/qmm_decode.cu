@@ -69,14 +69,15 @@ __global__ void __launch_bounds__(kDecThreads) embed_q8_kernel(const uint8_t* __
 
 // y = x / sqrt(mean(x^2) + eps) * (w + offset), one CTA per row.
 __global__ void __launch_bounds__(kDecThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                              float offset, float eps, int dim, float* __restrict__ y) {
+                                                              float offset, float eps, int dim, float* __restrict__ y,
+                                                              int ldy) {
     __shared__ float red[kDecThreads / 32];
     const float* xr = x + (size_t)blockIdx.x * dim;
     float ss = 0.0f;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += xr[i] * xr[i];
     ss = block_sum(ss, red);
     const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) y[(size_t)blockIdx.x * dim + i] = (xr[i] * inv) * (w[i] + offset);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) y[(size_t)blockIdx.x * ldy + i] = (xr[i] * inv) * (w[i] + offset);
 }
 
 // x += rmsnorm(branch) * (w_post + offset); then, if w_next, h = rmsnorm(x) *
@@ -89,9 +90,11 @@ __global__ void __launch_bounds__(kDecThreads) residual_norm_kernel(float* __res
                                                                     const float* __restrict__ branch,
                                                                     const float* __restrict__ w_post,
                                                                     const float* __restrict__ w_next, float offset,
-                                                                    float eps, int dim, float* __restrict__ h) {
+                                                                    float eps, int dim, float* __restrict__ h,
+                                                                    int ldh) {
     __shared__ float red[kDecThreads / 32];
     const size_t r0 = (size_t)blockIdx.x * dim;
+    const size_t hr0 = (size_t)blockIdx.x * ldh;  // h rows may be wider (a zero tail the kernel leaves alone)
     if (dim <= kNormRegs * kDecThreads) {
         float br[kNormRegs], xr[kNormRegs], wp[kNormRegs], wn[kNormRegs];
 #pragma unroll
@@ -122,7 +125,7 @@ __global__ void __launch_bounds__(kDecThreads) residual_norm_kernel(float* __res
 #pragma unroll
         for (int j = 0; j < kNormRegs; ++j) {
             const int i = threadIdx.x + j * kDecThreads;
-            if (i < dim) h[r0 + i] = (xr[j] * inv2) * (wn[j] + offset);
+            if (i < dim) h[hr0 + i] = (xr[j] * inv2) * (wn[j] + offset);
         }
         return;
     }
@@ -139,7 +142,7 @@ __global__ void __launch_bounds__(kDecThreads) residual_norm_kernel(float* __res
     if (w_next == nullptr) return;
     ss2 = block_sum(ss2, red);
     const float inv2 = 1.0f / sqrtf(ss2 / (float)dim + eps);
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) h[r0 + i] = (x[r0 + i] * inv2) * (w_next[i] + offset);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) h[hr0 + i] = (x[r0 + i] * inv2) * (w_next[i] + offset);
 }
 
 // One warp per head vector of one token: q heads get RMSNorm (q_norm) and
@@ -488,17 +491,18 @@ cudaError_t launch_embed_q8(const uint8_t* emb, int hidden, const int* tokens, i
     note_launch();
     return cudaGetLastError();
 }
-cudaError_t launch_rmsnorm(const float* x, const float* w, float offset, float eps, int rows, int dim, float* y,
+cudaError_t launch_rmsnorm(const float* x, const float* w, float offset, float eps, int rows, int dim, float* y, int ldy,
                            cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<rows, kDecThreads, 0, st>>>(x, w, offset, eps, dim, y);
+    rmsnorm_kernel<<<rows, kDecThreads, 0, st>>>(x, w, offset, eps, dim, y, ldy < dim ? dim : ldy);
     note_launch();
     return cudaGetLastError();
 }
 cudaError_t launch_residual_norm(float* x, const float* branch, const float* w_post, const float* w_next, float offset,
-                                 float eps, int rows, int dim, float* h, cudaStream_t st) {
+                                 float eps, int rows, int dim, float* h, int ldh, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    residual_norm_kernel<<<rows, kDecThreads, 0, st>>>(x, branch, w_post, w_next, offset, eps, dim, h);
+    residual_norm_kernel<<<rows, kDecThreads, 0, st>>>(x, branch, w_post, w_next, offset, eps, dim, h,
+                                                                     ldh < dim ? dim : ldh);
     note_launch();
     return cudaGetLastError();
 }

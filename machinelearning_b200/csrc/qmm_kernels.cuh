@@ -38,10 +38,10 @@ cudaError_t launch_gated_act(int kind, const float* gate, const float* up, int64
 // ---- decode-step pieces around the matmuls (qmm_decode.cu) ----------------------
 cudaError_t launch_embed_q8(const uint8_t* emb, int hidden, const int* tokens, int batch, int vocab, float scale,
                             float* x, cudaStream_t st);
-cudaError_t launch_rmsnorm(const float* x, const float* w, float offset, float eps, int rows, int dim, float* y,
+cudaError_t launch_rmsnorm(const float* x, const float* w, float offset, float eps, int rows, int dim, float* y, int ldy,
                            cudaStream_t st);
 cudaError_t launch_residual_norm(float* x, const float* branch, const float* w_post, const float* w_next, float offset,
-                                 float eps, int rows, int dim, float* h, cudaStream_t st);
+                                 float eps, int rows, int dim, float* h, int ldh, cudaStream_t st);
 cudaError_t launch_qk_rope_cache(const float* qkv, int batch, int nq, int nkv, int hd, const float* qn_w,
                                  const float* kn_w, float offset, float eps, const float* cos_t, const float* sin_t,
                                  const int* pos_dev, int ctx, float* q_out, float* k_cache, float* v_cache,

@@ -170,11 +170,12 @@ class Gemma3Decoder:
         P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         ck = _lib.check
         ck(L.qmm_embed_q8_dev(ctypes.c_void_p(self.emb.device_ptr()), cfg.vocab, H, P(self.tokens), B, cfg.emb_scale, P(self.x), sp))
-        ck(L.qmm_rmsnorm_dev(P(self.x), P(self.layers[0]["attn_norm"]), cfg.offset, cfg.eps, B, H, P(self.h), sp))
+        # normed hidden states go straight into hp (rows kh wide, zero tail)
+        ck(L.qmm_rmsnorm_dev(P(self.x), P(self.layers[0]["attn_norm"]), cfg.offset, cfg.eps, B, H, P(self.hp), self.kh,
+                             sp))
         for li, lw in enumerate(self.layers):
             theta = cfg.rope_global if (li + 1) % cfg.pattern == 0 else cfg.rope_local
             cos, sin = self.rope[theta]
-            self._pad_h()
             ck(L.qmm_linear_forward(lw["qkv"].handle, P(self.hp), B, P(self.qkv), 0, sp))
             if self.fused_attention:
                 ck(L.qmm_attention_decode_fused_dev(P(self.qkv), B, nq, nkv, hd, P(lw["q_norm"]), P(lw["k_norm"]),
@@ -189,25 +190,18 @@ class Gemma3Decoder:
                                               P(self.pos), cfg.ctx, self.inv_scale, P(self.part), P(self.attn), sp))
             ck(L.qmm_linear_forward(lw["o"].handle, P(self.attn), B, P(self.o), 0, sp))
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_attn_norm"]), P(lw["ffn_norm"]),
-                                          cfg.offset, cfg.eps, B, H, P(self.h), sp))
-            self._pad_h()
+                                          cfg.offset, cfg.eps, B, H, P(self.hp), self.kh, sp))
             ck(L.qmm_gated_forward(lw["gate_up"].handle, P(self.hp), B, P(self.ff), GELU, sp))
             ck(L.qmm_linear_forward(lw["down"].handle, P(self.ff), B, P(self.o), 0, sp))
             nxt = self.layers[li + 1]["attn_norm"] if li + 1 < len(self.layers) else self.final_norm
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_ffn_norm"]), P(nxt), cfg.offset, cfg.eps,
-                                          B, H, P(self.h), sp))
-        self._pad_h()
-        if self.hl is not self.hp:
+                                          B, H, P(self.hp), self.kh, sp))
+        if self.hl is not self.hp:  # batch 1: only the lm_head reads a padded copy
             with torch.cuda.stream(self.stream):
-                self.hl[:, :H].copy_(self.h)
+                self.hl[:, :H].copy_(self.hp)
         ck(L.qmm_linear_forward(self.lm_head.handle, P(self.hl), B, P(self.logits), 0, sp))
         if advance:
             ck(L.qmm_add_int_dev(P(self.pos), 1, sp))
-
-    def _pad_h(self) -> None:
-        if self.hp is not self.h:
-            with torch.cuda.stream(self.stream):
-                self.hp[:, :self.cfg.hidden].copy_(self.h)
 
     def set_position(self, pos: int) -> None:
         if not 0 <= pos < self.cfg.ctx:

@@ -63,6 +63,19 @@ QMM_API int qmm_device_count(void);
 /* Reads and clears the device-side error word of `device` (0 = none, 1 = a
  * bounded wait timed out). Synchronises the device. */
 QMM_API int qmm_device_error(int device, int* out_error);
+/* The same check as a status: synchronises `device`, reads and clears its
+ * error word, and returns QMM_OK, or QMM_ERR_TIMEOUT when a bounded wait of a
+ * kernel gave up since the last check (the reference's FFI turns every
+ * failure into a code, ffi/main/src/lib.rs:15-21). */
+QMM_API int qmm_device_status(int device);
+/* Launches, on `stream`, one wait on a shared-memory barrier that nothing
+ * completes, bounded to `probes` probes (1..2^20) instead of the library's
+ * 2^20, after which the kernel records a timeout in the error word and
+ * returns, as every wait of the hot path does. For testing the timeout path
+ * without hanging or faulting a GPU: qmm_device_status then reports
+ * QMM_ERR_TIMEOUT and the context stays usable. No counterpart in the
+ * reference (a CPU library). */
+QMM_API int qmm_selftest_bounded_wait(unsigned probes, void* stream);
 /* Number of kernel launches this library has issued in this process (stream
  * captures included), for launch accounting in benchmarks. No counterpart in
  * the reference (a CPU library). */
@@ -209,7 +222,10 @@ QMM_API int qmm_matmul_dev(int dtype, int act, const float* x_dev, const uint8_t
  * QMM_ERR_INVALID_INPUT. The first call on a device, with that device current,
  * looks the array's address up (make it before any stream capture). The array
  * is shared: calls that overlap on the GPU race, so keep them ordered (one
- * stream, or explicit synchronisation). Arguments as qmm_matmul_dev. */
+ * stream, or explicit synchronisation). It runs the GEMV kernels only (rows
+ * in chunks of at most 64): calls with 17 or more rows of f32 activations,
+ * which qmm_matmul_dev sends to the tensor-core GEMM, are slower here.
+ * Arguments as qmm_matmul_dev. */
 #define QMM_NOALLOC_SCRATCH_BYTES (4u << 20)
 QMM_API int qmm_matmul_dev_noalloc(int dtype, int act, const float* x_dev, const uint8_t* w_dev, size_t w_len,
                                    size_t m, size_t k, size_t n, float* y_dev, void* stream);

@@ -50,6 +50,8 @@ SIGNATURES = {
     "qmm_last_error_message": (ctypes.c_char_p, []),
     "qmm_device_count": (_I, []),
     "qmm_device_error": (_I, [_I, _P]),
+    "qmm_device_status": (_I, [_I]),
+    "qmm_selftest_bounded_wait": (_I, [ctypes.c_uint, _P]),
     "qmm_launch_count": (ctypes.c_ulonglong, []),
     "qmm_checksum_dev": (_I, [_P, _SZ, _P, _P]),
     "qmm_weight_checksum": (_I, [_P, _P]),

@@ -39,6 +39,21 @@ __device__ unsigned long long g_qmm_checksum_acc = 0;
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 static __device__ __align__(256) uint8_t g_qmm_noalloc_scratch[kNoAllocScratchBytes];
 
+// Self-test of the bounded-wait path (qmm_selftest_bounded_wait): one thread
+// waits on a freshly initialised mbarrier that nothing ever completes, with
+// the library's own probe loop cut to `probes`, then records the timeout in
+// the error word exactly as a kernel of the hot path would, and returns. It
+// cannot hang: the loop is bounded and no other thread waits on it.
+__global__ void selftest_wait_kernel(uint32_t probes, int* err) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    qmm::mbar_init(&bar, 1);
+    qmm::fence_mbar_init();
+    bool done = false;
+    for (uint32_t i = 0; i < probes && !done; ++i) done = qmm::mbar_try_wait(&bar, 0);
+    if (!done && err) atomicExch(err, qmm::kErrWaitTimeout);
+}
+
 namespace {
 
 thread_local std::string t_last_error;
@@ -390,7 +405,28 @@ QMM_API int qmm_device_error(int device, int* out_error) {
     return QMM_OK;
 }
 
-#define QMM_HOST_MATMUL(name, dt, native)                                                                      \
+QMM_API int qmm_device_status(int device) {
+    int v = 0;
+    int rc = qmm_device_error(device, &v);
+    if (rc) return rc;
+    if (v == kErrWaitTimeout) return fail(QMM_ERR_TIMEOUT, "a bounded device-side wait timed out");
+    if (v != kErrNone) return fail(QMM_ERR_CUDA, "device error word " + std::to_string(v));
+    return QMM_OK;
+}
+
+QMM_API int qmm_selftest_bounded_wait(unsigned probes, void* stream) {
+    if (probes == 0 || probes > kMaxWaitProbes) return fail(QMM_ERR_INVALID_INPUT, "probes outside 1..2^20");
+    const int dev = current_device();
+    if (dev < 0) return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    int* err = device_error_word(dev);
+    if (!err) return fail(QMM_ERR_CUDA, "device error word unavailable");
+    selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(probes, err);
+    note_launch();
+    QMM_CUDA(cudaGetLastError());
+    return QMM_OK;
+}
+
+#define QMM_HOST_MATMUL(name, dt, native)                                                                    \
     QMM_API int name(const float* input_data, size_t input_len, const uint8_t* weight_bytes, size_t weight_len, \
                      size_t m, size_t in_features, size_t out_features, float* output) {                       \
         return host_matmul(dt, native, input_data, input_len, weight_bytes, weight_len, m, in_features,       \
@@ -705,8 +741,14 @@ QMM_API int qmm_linear_forward_host(const qmm_weight* w, const float* x_host, si
 //    are cleared by each call's first kernel; everything else is overwritten
 //    before it is read. Calls that overlap on the GPU (different streams, or
 //    different host threads without ordering) race on it.
-//  * Calls no cudaMalloc/cudaFree and no heap-allocating routine: no caches,
-//    the tensor map is encoded on the stack each call.
+//  * Calls no cudaMalloc/cudaFree and no heap-allocating routine: the tensor
+//    map is encoded on the stack each call, and the planner's occupancy
+//    answers live in fixed-size tables (filled by the first call per kernel
+//    and shared-memory size, which also raises that kernel's shared-memory
+//    limit -- another reason to make the first calls before any capture).
+//  * Runs the GEMV kernels only (M in chunks of at most 64 rows): calls with
+//    17 or more f32-activation rows, which qmm_matmul_dev sends to the
+//    tensor-core GEMM when the row pitch allows, are slower here.
 namespace {
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;

@@ -319,7 +319,9 @@ int band_capacity(int qt, int M, size_t smem) {
         if (e.dev == dev && e.fn == fn && e.smem == smem) return e.cap;
     }
     int cap = 0;
-    if (ensure_dynamic_smem(fn, smem) == cudaSuccess) {
+    // raised directly (not through ensure_dynamic_smem's map): this query runs
+    // inside the allocation-free entry point too, and its answer is cached here
+    if (set_max_dynamic_smem(fn) == cudaSuccess) {
         int per_sm = 0, sms = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, band_threads(), smem) == cudaSuccess &&
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)

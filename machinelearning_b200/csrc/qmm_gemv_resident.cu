@@ -291,7 +291,9 @@ int resident_capacity(int qt, int loader, int nt, int cluster, size_t smem) {
         if (e.dev == dev && e.fn == fn && e.cluster == cluster && e.smem == smem) return e.cap;
     }
     int cap = 0;
-    if (ensure_dynamic_smem(fn, smem) == cudaSuccess) {
+    // raised directly (not through ensure_dynamic_smem's map): this query runs
+    // inside the allocation-free entry point too, and its answer is cached here
+    if (set_max_dynamic_smem(fn) == cudaSuccess) {
         if (cluster == 1) {
             int per_sm = 0, sms = 0;
             if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) == cudaSuccess &&

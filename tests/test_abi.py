@@ -95,3 +95,10 @@ def test_python_mirror_raises_reference_errors(qlib):
         kernel.quantize_q8_0(np.ones(33, np.float32))
     with pytest.raises(kernel.ShapeMismatch):
         kernel.matmul_f32_q8(np.ones(64, np.float32), np.zeros(10, np.uint8), 1, 64, 4)
+
+
+def test_selftest_rejects_bad_probe_counts(qlib):
+    """Argument checks happen before any device work (runs without a GPU)."""
+    from machinelearning_b200 import _lib
+    assert qlib.qmm_selftest_bounded_wait(0, None) == _lib.ERR_INVALID_INPUT
+    assert qlib.qmm_selftest_bounded_wait((1 << 20) + 1, None) == _lib.ERR_INVALID_INPUT

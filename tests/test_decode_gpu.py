@@ -102,3 +102,67 @@ def test_decode_cache_and_attention_pieces(oracle, torch_cuda):
         np.testing.assert_allclose(v_dev[li], vc[li], rtol=2e-3, atol=2e-4)
     assert not k_dev[:, :, :, :3].any() and not k_dev[:, :, :, 4:].any()
     model.close()
+
+
+# ---- BASELINE configs[3] at its own shapes --------------------------------------------------
+# Gemma-3-1B: 26 layers, hidden 1152, 4 query heads / 1 KV head of 256, GeGLU
+# 6912, tied Q8_0 vocabulary 262144, KV context 512. The cache is pre-filled
+# with the same random keys/values on both sides (positions before the step),
+# so a step at position p attends over p + 1 entries: p = 0 (one entry), 31 /
+# 32 (either side of a 32-position attention chunk), 511 (the full context,
+# 16 chunks). Batch 1 runs the resident / band GEMVs and the 262144-row padded
+# lm_head, batch 16 the two-token-tile GEMVs, batch 64 the tensor-core GEMM on
+# zero-padded rows.
+
+@pytest.fixture(scope="module")
+def gemma_1b(torch_cuda, oracle):
+    from machinelearning_b200.decode import Gemma3Config, random_weights
+    cfg = Gemma3Config.gemma3_1b(ctx=512)
+    w = random_weights(cfg, seed=4242, device=0)
+    host = {"emb": w["emb"].cpu().numpy(), "final_norm": w["final_norm"].cpu().numpy(),
+            "layers": [{k: v.cpu().numpy() for k, v in lw.items()} for lw in w["layers"]]}
+    return cfg, w, host
+
+
+def _prefill_cache(cfg, B, pos, seed):
+    """Random cache contents for positions < pos (zero elsewhere), shaped
+    [layers][B][n_kv][ctx][head_dim] like the decoder's cache."""
+    rng = np.random.default_rng(seed)
+    shape = (cfg.n_layers, B, cfg.n_kv_heads, cfg.ctx, cfg.head_dim)
+    k = np.zeros(shape, np.float32)
+    v = np.zeros(shape, np.float32)
+    if pos:
+        k[:, :, :, :pos] = rng.standard_normal((cfg.n_layers, B, cfg.n_kv_heads, pos, cfg.head_dim), np.float32)
+        v[:, :, :, :pos] = rng.standard_normal((cfg.n_layers, B, cfg.n_kv_heads, pos, cfg.head_dim),
+                                               np.float32) * np.float32(0.7)
+    return k, v
+
+
+@pytest.mark.parametrize("B,positions", [(1, (0, 31, 32, 511)), (16, (0, 31, 511)), (64, (32, 511))])
+def test_gemma3_1b_decode_at_config_shapes(gemma_1b, torch_cuda, oracle, B, positions):
+    from conftest import assert_close_rel
+    from oracle.decode import decode_step
+
+    from machinelearning_b200.decode import Gemma3Decoder
+    cfg, w, host = gemma_1b
+    model = Gemma3Decoder(cfg, w, batch=B)
+    rng = np.random.default_rng(77 + B)
+    try:
+        for pos in positions:
+            kc, vc = _prefill_cache(cfg, B, pos, seed=1000 * B + pos)
+            model.k_cache.copy_(torch_cuda.from_numpy(kc))
+            model.v_cache.copy_(torch_cuda.from_numpy(vc))
+            model.set_position(pos)
+            tokens = rng.integers(0, cfg.vocab, B)
+            got = model.step(tokens).cpu().numpy()
+            ref = decode_step(cfg, host, tokens, pos, list(kc), list(vc))
+            # the GEMV paths (batch 1, 16) carry activations as f16 hi + lo;
+            # the GEMM (batch 64) rounds both operands to f16 once per matmul
+            gemm = model.kh != cfg.hidden
+            rel = assert_close_rel(got.ravel(), ref.ravel(), 1e-3, 1e-2 if gemm else None)
+            print(f"batch {B} position {pos}: norm-wise relative error {rel:.2e}")
+            # the step wrote the reference's k / v at the position
+            kd = model.k_cache[:, :, :, pos].cpu().numpy()
+            np.testing.assert_allclose(kd, kc[:, :, :, pos], rtol=2e-3, atol=2e-3 if gemm else 2e-4)
+    finally:
+        model.close()

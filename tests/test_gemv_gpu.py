@@ -486,3 +486,85 @@ def test_linear_forward_host_pinned(oracle, torch_cuda, qlib, m, k, n):
 
 def test_no_device_error_recorded(torch_cuda, qlib):
     assert device_error_clear(qlib) == 0
+
+
+# ---- BASELINE configurations in the modes not covered above --------------------------------
+
+def test_config3_prefill_q4_0_native_row_subset(oracle, torch_cuda, qlib):
+    """BASELINE configs[2] in the Q8_0-activation mode (matmul_f32_q4_native,
+    reference quantize.rs:714-772: every token row quantised by
+    quantize_row_q8_0, integer block dots scaled in the reference's order):
+    M = 512, K = 4096, N = 11008 on the device, bit-exact against the oracle on
+    three spreads of output rows (rows are independent dot products, so a
+    subset of weight rows gives exactly those outputs)."""
+    m, k, n = 512, 4096, 11008
+    w = make_weights(oracle, Q4_0, n, k, seed=3)
+    x = np.random.default_rng(301).normal(0, 1, m * k).astype(np.float32)
+    y = gpu_matmul(torch_cuda, qlib, Q4_0, 1, x, w, m, k, n).reshape(m, n)
+    rb = (k // 32) * BB[Q4_0]
+    for r0, r1 in ((0, 256), (5000, 5256), (n - 256, n)):
+        ref = oracle.matmul_f32_q4_native(x, w[r0 * rb:r1 * rb], m, k, r1 - r0).reshape(m, r1 - r0)
+        assert_bits_equal(y[:, r0:r1], ref, f"rows {r0}..{r1}")
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_config5_lm_head_q8_0_m32_row_subsets(oracle, torch_cuda, qlib, act):
+    """BASELINE configs[4]'s Q8_0 lm_head 8192 -> 128256 at batch 32: f32
+    activations run the tensor-core GEMM (224-row weight tiles, ~3.9 waves),
+    Q8_0 activations the int8 GEMV (matmul_f32_q8_v2, bit-exact). The oracle
+    covers the first, a middle and the last (ragged) 2048 output rows."""
+    k, n, m = 8192, 128256, 32
+    w = random_blocks(Q8_0, n, k, seed=55)
+    x = np.random.default_rng(56).normal(0, 1, m * k).astype(np.float32)
+    y = gpu_matmul(torch_cuda, qlib, Q8_0, act, x, w, m, k, n).reshape(m, n)
+    rb = (k // 32) * 34
+    for r0 in (0, 61000, n - 2048):
+        wsub = w[r0 * rb:(r0 + 2048) * rb]
+        if act:
+            ref = oracle.matmul_f32_q8_v2(x, wsub, m, k, 2048).reshape(m, 2048)
+            assert_bits_equal(y[:, r0:r0 + 2048], ref, f"rows {r0}..")
+        else:
+            ref = oracle.matmul_f32_q8(x, wsub, m, k, 2048).reshape(m, 2048)
+            assert_close_rel(y[:, r0:r0 + 2048].ravel(), ref.ravel(), 1e-3,
+                             GEMM_ELEM_RTOL if gemm_path(Q8_0, 0, m, k) else None)
+
+
+def _q8_block(d_bits, q):
+    b = np.zeros(34, np.uint8)
+    b[0:2] = np.array([d_bits], np.uint16).view(np.uint8)
+    b[2:] = np.asarray(q, np.int8).view(np.uint8)
+    return b
+
+
+def _q4_block(d_bits, nib):
+    b = np.zeros(18, np.uint8)
+    b[0:2] = np.array([d_bits], np.uint16).view(np.uint8)
+    nib = np.asarray(nib, np.uint8)
+    b[2:] = (nib[:16] | (nib[16:] << 4)).astype(np.uint8)  # GGML order
+    return b
+
+
+def test_integer_kat_extremes_through_the_device(oracle, torch_cuda, qlib):
+    """The reference's integer known-answer extremes (simd.rs:833-851: a 32-wide
+    q8 x q8 block dot of all 127 x all 127 = 516128, 127 x -128 = -520192; the
+    q4 x q8 dot of nibbles 15 / 0 against 127 = 7 * 127 * 32 = 28448 /
+    -8 * 127 * 32 = -32512) reached through the device's Q8_0-activation
+    matmuls as 1 x 32 x 1 problems: activations of 1.0 quantise to q = 127,
+    weight scale d = 1.0 (f16 0x3C00). The outputs are dot * xs * ws in the
+    reference's order (quantize.rs:481, 706), bit-exact with the oracle, and
+    dividing by the scales recovers the integer exactly."""
+    one = np.ones(32, np.float32)
+    cases = [(Q8_0, _q8_block(0x3C00, [127] * 32), 516128),
+             (Q8_0, _q8_block(0x3C00, [-128] * 32), -520192),
+             (Q4_0, _q4_block(0x3C00, [15] * 32), 28448),
+             (Q4_0, _q4_block(0x3C00, [0] * 32), -32512)]
+    for dt, blk, dot in cases:
+        y = gpu_matmul(torch_cuda, qlib, dt, 1, one, blk, 1, 32, 1)
+        ref = getattr(oracle, ORACLE_FN[(dt, 1)])(one, blk, 1, 32, 1)
+        assert_bits_equal(y, ref, f"dt={dt} dot={dot}")
+        if dt == Q8_0:
+            xscale = np.float32(np.float16(np.float32(1.0) / np.float32(127.0)))  # f32(f16(amax / 127))
+        else:
+            xscale = oracle.quantize_row_q8_0(one)[1][0]
+        expect = np.float32(np.float32(np.float32(dot) * np.float32(xscale)) * np.float32(1.0))
+        assert y[0] == expect, (dt, dot, y[0], expect)

@@ -1,12 +1,12 @@
 """Benchmark of the quantized-matmul hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-sub]
                     [--workload gemma-q8-sweep|q4-gemv|llama70b|llama70b-gate|prefill|gemma-decode]
                     [--batch B]
 
 Workloads (synthetic, seeded, weights ~N(0, 0.02)
 quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
-  gemma-q8-sweep (default, configs[1]): the seven Gemma-3-1B projections
+  gemma-q8-sweep: the seven Gemma-3-1B projections
       (K->N) 1152->1024 q, 1152->256 k, 1152->256 v, 1024->1152 o,
       1152->6912 gate, 1152->6912 up, 6912->1152 down, Q8_0, each at batch 1
       and batch 8. One step = those 14 GEMVs. 26 distinct weight sets (one per
@@ -14,8 +14,13 @@ quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
       from HBM every step.
   q4-gemv: Q4_0 [6912 x 1152] x f32 [1152], batch 1, 64 weight
       copies rotated (287 MB > L2).
-  llama70b: Q4_0 gate/up 8192->28672, down 28672->8192, Q8_0
-      lm_head 8192->128256, batch 1 and 32 (1.5 GB of weights per batch).
+  llama70b (default, configs[4]): Q4_0 gate/up 8192->28672, down
+      28672->8192, Q8_0 lm_head 8192->128256, batch 1 and 32 (1.5 GB of
+      weights per batch) -- the configuration BASELINE defines at 1/2/4/8
+      GPUs. The default run (no --workload) prints its line with one
+      sub-record per other configuration under "workloads" (one GPU only):
+      gemma-q8-sweep, q4-gemv, prefill, gemma-decode at batch 1, 16 and 64,
+      each timed in the same run with its own roofline, e2e and CPU baseline.
   llama70b-gate (one projection of configs[4]): Q4_0 8192->28672, batch 1,
       two weight copies (264 MB > L2); the small case for streaming-kernel
       profiles.
@@ -195,8 +200,52 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+MIN_TIMED_S = 0.1  # every timed region is repeated until the repetitions cover this
+
+
+def timed_regions(enqueue, stream, dev, steps, world, sampler):
+    """Times `steps` steps with CUDA events on `stream` (enqueue(steps) issues
+    them), barrier + synchronize on both sides, max over ranks; the K-step
+    region is repeated until the repetitions cover MIN_TIMED_S (at least
+    once), and the median repetition is reported. Returns (ms of the median
+    region, every region's ms, clock samples taken during the regions)."""
+    import torch
+    import torch.distributed as dist
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def one():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            enqueue(steps)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:  # the same number of collectives on every rank
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    n_before = len(sampler.samples)
+    regions = [one()]
+    reps = max(1, int(MIN_TIMED_S * 1e3 / max(regions[0], 1e-3) + 0.999))
+    for _ in range(reps - 1):
+        regions.append(one())
+    n_timed = len(sampler.samples) - n_before
+    return statistics.median(regions), regions, n_timed
+
+
 # ---- our implementation -----------------------------------------------------------------
 def run_ours(args, rank, world, local_rank):
+    """One GEMV / GEMM workload (args.workload); returns rank 0's JSON record
+    (None on other ranks)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -271,71 +320,56 @@ def run_ours(args, rank, world, local_rank):
     steps_work = sum(work(wl, b, k, n, dt) for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems)
     metric, unit, div = metric_info(wl)
 
-    # ---- CUDA graphs: one per weight copy -------------------------------------------------
-    graphs = []
+    # ---- CUDA graphs ---------------------------------------------------------------------
+    # A timed region of K steps runs step i on weight copy i % copies: whole
+    # passes over the copies as one graph each, then one graph of the
+    # remaining K % copies steps (copies 0, 1, ...), so a region is at most
+    # K // copies + 1 graph launches whatever K is.
+    graphs = {}
     with torch.cuda.stream(stream):
         for c in range(copies):
             one_step(c)  # warm the planner/tensor-map caches outside capture
         stream.synchronize()
-        for c in range(copies):
+
+        def capture(n):
             g = torch.cuda.CUDAGraph()
             n0 = L.qmm_launch_count()
             with torch.cuda.graph(g, stream=stream):
-                one_step(c)
-            launches_per_step = L.qmm_launch_count() - n0
-            graphs.append(g)
-        # one graph per full pass over the weight copies (fewer graph launches:
-        # no launch gap between the steps of a pass)
-        pass_graph = None
-        if copies > 1:
-            pass_graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(pass_graph, stream=stream):
-                for c in range(copies):
+                for c in range(n):
                     one_step(c)
+            return g, L.qmm_launch_count() - n0
+
+        g1, launches_per_step = capture(1)
+        graphs[1] = g1
+        for n in {copies, args.steps % copies, args.warmup % copies}:
+            if n > 1 and n not in graphs:
+                graphs[n] = capture(n)[0]
     torch.cuda.synchronize(dev)
 
     def run_steps(n):
-        """Exactly n steps, step i on weight copy i % copies: whole passes
-        where they fit, single-step graphs for the rest."""
-        i = 0
-        while i < n:
-            if pass_graph is not None and i % copies == 0 and i + copies <= n:
-                pass_graph.replay()
-                i += copies
-            else:
-                graphs[i % copies].replay()
-                i += 1
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+        """Exactly n steps, step i on weight copy i % copies."""
+        for _ in range(n // copies):
+            graphs[copies].replay()
+        r = n % copies
+        if r in graphs:
+            graphs[r].replay()
+        else:
+            for _ in range(r):  # (only for counts no graph was captured for)
+                graphs[1].replay()
 
     # warm-up
     with torch.cuda.stream(stream):
         run_steps(args.warmup)
     stream.synchronize()
 
-    # timed region: K steps, events on the launching stream, max over ranks
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # timed regions: K steps each, events on the launching stream, max over
+    # ranks, repeated to >= 100 ms, median reported
     sampler = ClockSampler(local_rank)
     with sampler:
         with torch.cuda.stream(stream):
             run_steps(max(args.warmup, 3))  # clock soak right before the timed region
-        barrier()
         torch.cuda.synchronize(dev)
-        n_before = len(sampler.samples)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            run_steps(args.steps)
-            e1.record(stream)
-        torch.cuda.synchronize(dev)
-        barrier()
-        n_timed = len(sampler.samples) - n_before
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, regions, n_timed = timed_regions(run_steps, stream, dev, args.steps, world, sampler)
     ms_per_step = ms / args.steps
     value = steps_work * args.steps / (ms / 1e3) / div
 
@@ -352,7 +386,7 @@ def run_ours(args, rank, world, local_rank):
     clocks["samples_in_timed_region"] = n_timed
     # graphs that hold NCCL calls are released before the process group goes
     graphs.clear()
-    pass_graph = None
+    line = None
     if rank == 0:
         line = {
             "metric": metric,
@@ -379,7 +413,7 @@ def run_ours(args, rank, world, local_rank):
                 "l2": f"{copies} weight copies rotated" + (" (>L2)" if copies > 1 else "; weights > L2"),
                 "algorithmic_bytes_per_step": steps_bytes,
                 "algorithmic_flops_per_step": sum(2 * b * k * n for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems),
-                "graph": "one CUDA graph per pass over the weight copies (single-step graphs for the rest of K); "
+                "graph": "one CUDA graph per pass over the weight copies plus one for the remaining K % copies steps; "
                          "PDL between kernels",
             },
             "roofline": {
@@ -398,10 +432,15 @@ def run_ours(args, rank, world, local_rank):
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
+            "timed_regions": {"count": len(regions), "ms_each": [round(r, 4) for r in regions[:8]],
+                              "total_ms": round(sum(regions), 3),
+                              "rule": f"K-step region repeated to >= {MIN_TIMED_S * 1e3:.0f} ms, median reported"},
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+    del weights, xs, ys, gathered
+    torch.cuda.empty_cache()
+    return line
 
 
 def run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies):
@@ -618,23 +657,31 @@ def decode_bytes(cfg, batch, weights_bytes):
     return weights_bytes + kv + batch * (cfg.hidden // 32) * 34 + batch * cfg.vocab * 4
 
 
-def _decode_setup(args, local_rank, rank):
+def decode_weight_bytes(cfg):
+    """Algorithmic weight bytes of one decode step: every Q4_0 layer matrix and
+    the Q8_0 lm_head once, unpadded (the GGUF bytes)."""
+    H, nq, nkv, hd = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    per_layer = ((nq + 2 * nkv) * hd * H + H * nq * hd + 2 * cfg.ffn * H + H * cfg.ffn) // 32 * 18
+    return cfg.n_layers * per_layer + cfg.vocab * (H // 32) * 34
+
+
+def _decode_weights(local_rank, rank):
+    from machinelearning_b200.decode import Gemma3Config, random_weights
+    cfg = Gemma3Config.gemma3_1b(ctx=512)
+    return cfg, random_weights(cfg, seed=1234 + rank, device=local_rank)
+
+
+def run_decode(args, rank, world, local_rank, shared=None):
+    """Decode tokens/s of the Gemma-3-1B step (one graph replay per step at
+    position 511, batch args.batch). N > 1: one independent replica per GPU.
+    shared: (cfg, weights) to reuse across batches. Returns rank 0's record."""
+    import numpy as np
     import torch
 
-    from machinelearning_b200.decode import Gemma3Config, Gemma3Decoder, random_weights
-    cfg = Gemma3Config.gemma3_1b(ctx=512)
-    w = random_weights(cfg, seed=1234 + rank, device=local_rank)
-    model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank)
-    wbytes = model.lm_head.nbytes + sum(l[k].nbytes for l in model.layers for k in ("qkv", "o", "gate_up", "down"))
-    return cfg, w, model, wbytes, torch
-
-
-def run_decode(args, rank, world, local_rank):
-    """Decode tokens/s of the Gemma-3-1B step (one graph replay per step at
-    position 511, batch args.batch). N > 1: one independent replica per GPU."""
-    import numpy as np
     from machinelearning_b200 import _lib
-    cfg, w, model, wbytes, torch = _decode_setup(args, local_rank, rank)
+    from machinelearning_b200.decode import Gemma3Decoder
+    cfg, w = shared if shared is not None else _decode_weights(local_rank, rank)
+    model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank)
     L = _lib.lib()
     dev = model.dev
     B = args.batch
@@ -651,30 +698,20 @@ def run_decode(args, rank, world, local_rank):
         for _ in range(args.warmup):
             model.graph.replay()
     torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def enqueue(n):
+        for _ in range(n):
+            model.graph.replay()
+
     sampler = ClockSampler(local_rank)
     with sampler:
         with torch.cuda.stream(st):
-            for _ in range(max(args.warmup, 3)):
-                model.graph.replay()
+            enqueue(max(args.warmup, 3))
         torch.cuda.synchronize(dev)
-        n_before = len(sampler.samples)
-        with torch.cuda.stream(st):
-            e0.record(st)
-            for _ in range(args.steps):
-                model.graph.replay()
-            e1.record(st)
-        torch.cuda.synchronize(dev)
-        n_timed = len(sampler.samples) - n_before
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, regions, n_timed = timed_regions(enqueue, st, dev, args.steps, world, sampler)
     ms_per_step = ms / args.steps
     value = B * world * args.steps / (ms / 1e3)
-    step_bytes = decode_bytes(cfg, B, wbytes)
+    step_bytes = decode_bytes(cfg, B, decode_weight_bytes(cfg))
     achieved = step_bytes / (ms_per_step / 1e3) / 1e9
 
     e2e = None
@@ -707,6 +744,7 @@ def run_decode(args, rank, world, local_rank):
     clocks = sampler.summary()
     clocks["samples_in_timed_region"] = n_timed
     model.close()
+    line = None
     if rank == 0:
         line = {
             "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -715,21 +753,25 @@ def run_decode(args, rank, world, local_rank):
             "dtype": "f32 activations and KV cache x Q4_0 linears / Q8_0 lm_head (f16 tensor-core MMA, f32 accumulate)",
             "data": "synthetic: random-init weights ~N(0,0.02) quantised on device, norm vectors ~N(0,0.1), "
                     "seeded token ids uniform in the vocabulary",
-            "config": {"workload": args.workload, "baseline_config_index": 3, "model": WORKLOADS["gemma-decode"]["model"],
+            "config": {"workload": "gemma-decode", "baseline_config_index": 3,
+                       "model": WORKLOADS["gemma-decode"]["model"],
                        "batch": B, "position": DECODE_POS, "kv_context": cfg.ctx,
                        "parallelism": f"{world} replicas" if world > 1 else "single",
                        "graph": "one CUDA graph per step (embedding, 26 layers, final norm, lm_head)",
                        "l2": "weights 0.71 GB > L2", "bytes_per_step": step_bytes},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profiled_traffic(args.workload),
-                         "note": "achieved = weight bytes + KV bytes read + embedding rows + logits per step / step "
-                                 "time (CUDA events on the replay stream)"},
+                         "traffic": profiled_traffic("gemma-decode"),
+                         "note": "achieved = weight bytes (unpadded GGUF bytes) + KV bytes read + embedding rows + "
+                                 "logits per step / step time (CUDA events on the replay stream)"},
             "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clocks,
+            "timed_regions": {"count": len(regions), "ms_each": [round(r, 4) for r in regions[:8]],
+                              "total_ms": round(sum(regions), 3),
+                              "rule": f"K-step region repeated to >= {MIN_TIMED_S * 1e3:.0f} ms, median reported"},
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+    return line
 
 
 def _decode_host_weights(w):
@@ -771,9 +813,9 @@ def run_decode_reference(args, rank, world):
         return
     import oracle
     oracle.build()
-    cfg, w, model, wbytes, torch = _decode_setup(args, int(os.environ.get("LOCAL_RANK", "0")), 0)
+    cfg, w = _decode_weights(int(os.environ.get("LOCAL_RANK", "0")), 0)
     hw = _decode_host_weights(w)
-    model.close()
+    del w
     steps = max(1, min(args.steps, 3))
     s = decode_cpu_time(cfg, hw, args.batch, steps)
     value = args.batch / s
@@ -789,48 +831,13 @@ def run_decode_reference(args, rank, world):
         "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
-def main(argv=None):
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemma-q8-sweep")
-    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
-    ap.add_argument("--batch", type=int, default=1, help="gemma-decode: sequences per step (1, 16, 64)")
-    ap.add_argument("--copies", type=int, default=None,
-                    help="weight copies rotated (default: the workload's; fewer for short profiling runs)")
-    args = ap.parse_args(argv)
-    if args.warmup < 3:
-        args.warmup = 3
+DEFAULT_WORKLOAD = "llama70b"  # the configuration defined at 1/2/4/8 GPUs
+# the other BASELINE configurations, timed in the same default run (one GPU)
+SUB_WORKLOADS = [("gemma-q8-sweep", None), ("q4-gemv", None), ("prefill", None), ("gemma-decode", 1),
+                 ("gemma-decode", 16), ("gemma-decode", 64)]
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.workload == "gemma-decode":
-        if args.impl == "reference":
-            run_decode_reference(args, rank, world)
-            return 0
-        if world > 1:
-            import datetime
 
-            import torch
-            import torch.distributed as dist
-            torch.cuda.set_device(local_rank)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", local_rank))
-        try:
-            run_decode(args, rank, world, local_rank)
-        finally:
-            if world > 1:
-                import torch.distributed as dist
-                dist.destroy_process_group()
-        return 0
-    if args.impl == "reference":
-        run_reference(args, rank, world)
-        return 0
+def _init_dist(world, local_rank):
     if world > 1:
         import datetime
 
@@ -839,8 +846,68 @@ def main(argv=None):
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+
+
+def _run_one(args, rank, world, local_rank, shared_decode=None):
+    if args.workload == "gemma-decode":
+        return run_decode(args, rank, world, local_rank, shared_decode)
+    return run_ours(args, rank, world, local_rank)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                    help=f"one workload only (default: {DEFAULT_WORKLOAD}, plus one sub-record per other BASELINE "
+                         "configuration on one GPU)")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
+    ap.add_argument("--no-sub", action="store_true", help="default run without the other configurations' records")
+    ap.add_argument("--batch", type=int, default=1, help="gemma-decode: sequences per step (1, 16, 64)")
+    ap.add_argument("--copies", type=int, default=None,
+                    help="weight copies rotated (default: the workload's; fewer for short profiling runs)")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    default_run = args.workload is None
+    if default_run:
+        args.workload = DEFAULT_WORKLOAD
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if args.workload == "gemma-decode":
+            run_decode_reference(args, rank, world)
+        else:
+            run_reference(args, rank, world)
+        return 0
+    _init_dist(world, local_rank)
     try:
-        run_ours(args, rank, world, local_rank)
+        line = _run_one(args, rank, world, local_rank)
+        if default_run and world == 1 and not args.no_sub:
+            # every other BASELINE configuration, timed in this same run
+            subs = {}
+            shared = None
+            for name, batch in SUB_WORKLOADS:
+                sub = argparse.Namespace(**vars(args))
+                sub.workload, sub.copies = name, None
+                if batch is not None:
+                    sub.batch = batch
+                    if shared is None:
+                        shared = _decode_weights(local_rank, rank)
+                rec = _run_one(sub, rank, world, local_rank, shared)
+                if rec is not None:
+                    subs[name if batch is None else f"{name}-b{batch}"] = rec
+            shared = None
+            if line is not None:
+                line["workloads"] = subs
+        if line is not None:
+            print(json.dumps(line), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist

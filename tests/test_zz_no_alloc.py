@@ -53,10 +53,11 @@ def _oracle(oracle, dt, act, x, w, m, k, n):
 #    side records, split-K partials and tickets in the scratch array;
 #  * Q8_0 f32, M = 1, 8192 -> 16384 (142 MB, too large for the resident
 #    kernel): the band GEMV with K split in two slices -> partials and tickets;
-#  * Q4_0 f32, M = 3, 4096 -> 96: the streaming GEMV, K split over warps;
+#  * Q4_0 f32, M = 24, 4096 -> 96: the streaming GEMV (more tokens than the
+#    resident kernel takes), K split over warps;
 #  * Q8_0 / Q4_0 with Q8_0 activations: the streaming GEMV's quantised
 #    activation records (these must match the reference bit for bit).
-CASES = [(Q8_0, 0, 20, 1152, 256, True), (Q8_0, 0, 1, 8192, 16384, True), (Q4_0, 0, 3, 4096, 96, True),
+CASES = [(Q8_0, 0, 20, 1152, 256, True), (Q8_0, 0, 1, 8192, 16384, True), (Q4_0, 0, 24, 4096, 96, True),
          (Q8_0, 1, 8, 1152, 1024, True), (Q4_0, 1, 1, 6912, 1152, True)]
 
 

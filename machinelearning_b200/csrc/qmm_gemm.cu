@@ -42,10 +42,13 @@
 
 #include "qmm_common.cuh"
 #include "qmm_kernels.cuh"
+#include "qmm_tcgen05.cuh"
 
 namespace qmm {
 
 namespace {
+
+using namespace tc;
 
 constexpr int BM = 128;            // tokens per accumulator (MMA M, TMEM lanes)
 constexpr int BN = 128;            // weight rows per tile by default (MMA N, TMEM columns); 160 also built
@@ -104,83 +107,6 @@ static_assert(gemm_smem_bytes(kQ4_0, 2, 160) <= 232448 && gemm_smem_bytes(kQ4_1,
                   gemm_smem_bytes(kQ8_0, 1, 64) <= 232448 && gemm_smem_bytes(kQ8_0, 2, 64) <= 232448 &&
                   gemm_smem_bytes(kQ8_0, 1, 224) <= 232448,
               "a GEMM variant exceeds 227 KB of shared memory");
-
-// ---- tcgen05 / TMEM --------------------------------------------------------------
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// D(tmem) (+)= A(smem desc) . B(smem desc)^T, f16 inputs, f32 accumulator.
-__device__ __forceinline__ void mma_f16_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrive on `bar` once every tcgen05.mma this thread issued has completed.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-// 32 consecutive TMEM columns of this warp's 32 lanes, one lane per thread;
-// the wait is tied to the registers so no use can move above it.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
-                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
-                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-                 :
-                 : "memory");
-}
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), leading offset unused for this layout (1), the
-// Blackwell descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both
-// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-__host__ __device__ constexpr uint32_t gemm_idesc(int W) {
-    return (1u << 4) | ((uint32_t)(W >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-// ---- dequantisation to f16 pairs --------------------------------------------------------
-__device__ __forceinline__ __half2 as_h2(uint32_t v) {
-    __half2 h;
-    memcpy(&h, &v, 4);
-    return h;
-}
-__device__ __forceinline__ uint32_t h2_u32(__half2 h) {
-    uint32_t v;
-    memcpy(&v, &h, 4);
-    return v;
-}
-__device__ __forceinline__ __half2 half2_from_bits(uint32_t bits16) {
-    const __half h = __ushort_as_half((unsigned short)bits16);
-    return __halves2half2(h, h);
-}
 
 // Q8_0: 4 int8 -> two f16 pairs d*q (elements in order).
 __device__ __forceinline__ void q8_pairs(uint32_t w, __half2 d2, uint32_t& p01, uint32_t& p23) {
@@ -673,8 +599,12 @@ cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 
 }  // namespace
 
+// Routing: decode batches (M <= kGemmTnMaxRows) run on the decode-batch GEMM
+// (qmm_gemm_tn.cu, exact operand split, 8-mod-16 row pitches too); larger M on
+// the prefill GEMM below.
 bool gemm_supported(int qt, bool native, int M, int N, int K) {
-    if (native || M < kGemmMinRows || N < 1 || K < QK || K % QK) return false;
+    if (gemm_tn_supported(qt, native, M, N, K)) return true;
+    if (native || M <= kGemmTnMaxRows || N < 1 || K < QK || K % QK) return false;
     const int bb = block_bytes(qt);
     if (!bb) return false;
     const int64_t row_bytes = (int64_t)(K / QK) * bb;
@@ -723,6 +653,7 @@ size_t x16_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((
 }  // namespace
 
 size_t gemm_workspace_bytes(int M, int N, int K, int qt) {
+    if (gemm_tn_supported(qt, false, M, N, K)) return gemm_tn_workspace_bytes(M, N, K, qt);
     const GemmPlan p = gemm_plan(qt, M, N, K);
     size_t b = x16_bytes(M, K);
     if (p.ks > 1) {
@@ -734,6 +665,8 @@ size_t gemm_workspace_bytes(int M, int N, int K, int qt) {
 
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws, int* err,
                         cudaStream_t st, bool weights_immutable, const GatedOut& g) {
+    if (gemm_tn_supported(qt, false, M, N, K))
+        return launch_gemm_tn(qt, w, x, y, M, N, K, ws, err, st, weights_immutable, g);
     __half* x16 = static_cast<__half*>(ws);
     float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256((size_t)M * K * 2));
     {

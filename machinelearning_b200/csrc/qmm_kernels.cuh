@@ -236,6 +236,16 @@ size_t gemm_workspace_bytes(int M, int N, int K, int qt);
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
                         int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut());
 
+// ---- decode-batch GEMM (qmm_gemm_tn.cu): tcgen05, weights on the MMA's M side,
+// tokens on its N side, exact hi/lo split of both operands (~1e-6 relative).
+// f32-activation calls with kGemmMinRows <= M <= kGemmTnMaxRows and a row
+// pitch of 0 or 8 mod 16 bytes (N even for the latter).
+constexpr int kGemmTnMaxRows = 128;
+bool gemm_tn_supported(int qt, bool native, int M, int N, int K);
+size_t gemm_tn_workspace_bytes(int M, int N, int K, int qt);
+cudaError_t launch_gemm_tn(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
+                           int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut());
+
 int* device_error_word(int device);
 
 // Launch accounting (qmm_launch_count): every launch site calls note_launch().

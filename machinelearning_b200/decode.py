@@ -90,13 +90,22 @@ def _quant_weight(dt: int, n: int, k: int, data, device: int, kpad: int = 0) -> 
 
 
 def padded_k(k: int, batch: int) -> int:
-    """Columns a batch-matmul weight of k columns is padded to: batches of 17
-    or more run on the tensor-core GEMM, which needs a 16-byte row pitch (Q4_0
-    and Q8_0 rows are 18 and 34 bytes per 32 columns: a multiple of 8 blocks);
-    smaller batches keep k."""
-    if batch < 17 or (k // 32) % 8 == 0:
+    """Columns a batch-matmul weight of k columns is padded to. Batches of 17
+    to 128 run on the decode-batch tensor-core GEMM, which reads row pitches
+    of 0 or 8 mod 16 bytes in place (Q4_0 / Q8_0 rows are 18 / 34 bytes per 32
+    columns: k/32 a multiple of 4); larger batches run on the prefill GEMM,
+    which needs a 16-byte pitch (k/32 a multiple of 8); smaller batches keep
+    k (GEMV)."""
+    nb = k // 32
+    if batch < 17 or nb % 8 == 0 or (batch <= 128 and nb % 4 == 0):
         return k
     return (k // 256 + 1) * 256
+
+
+def band_k(k: int) -> int:
+    """Columns the lm_head is padded to at batch 1: a 16-byte row pitch lets its
+    one-token matmul stream through the band GEMV."""
+    return k if (k // 32) % 8 == 0 else (k // 256 + 1) * 256
 
 
 class Gemma3Decoder:
@@ -120,7 +129,7 @@ class Gemma3Decoder:
         self.kh = kh = padded_k(H, batch)  # K of the matmuls that read the hidden state
         # the lm_head also at batch 1: a 16-byte row pitch lets its one-token
         # matmul stream through the band kernel
-        self.klm = klm = kh if batch != 1 else padded_k(H, 17)
+        self.klm = klm = kh if batch != 1 else band_k(H)
         self.lm_head = self.emb if klm == H else _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device, klm)
         self.final_norm = vec(weights["final_norm"])
         self.layers = []

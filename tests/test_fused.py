@@ -64,7 +64,9 @@ def _rows(oracle, dt, n, k, rng, scale=0.05):
 
 
 def _gemm(dt, m, k):
-    return m >= 17 and ((k // 32) * BB[dt]) % 16 == 0
+    """The prefill GEMM (f16 operands rounded once): M > 128, 16-byte row pitch.
+    Decode batches of 17-128 run the decode-batch GEMM (exact operand split)."""
+    return m > 128 and ((k // 32) * BB[dt]) % 16 == 0
 
 
 def _interleave(gate, up, hidden, k, dt):
@@ -122,16 +124,16 @@ GATED = [  # (dtype, hidden, in, m, act)
     (Q8_0, 6912, 1152, 1, GELU),    # Gemma-3-1B MLP, decode
     (Q8_0, 6912, 1152, 4, GELU),
     (Q8_0, 6912, 1152, 16, SILU),
-    (Q8_0, 6912, 1152, 17, GELU),   # GEMV (1224-byte rows)
-    (Q8_0, 6912, 1152, 100, GELU),  # two GEMV row chunks
+    (Q8_0, 6912, 1152, 17, GELU),   # decode-batch GEMM, paired rows (1224-byte pitch)
+    (Q8_0, 6912, 1152, 100, GELU),  # decode-batch GEMM, 128-token tile
     (Q4_0, 6912, 1152, 1, SILU),
     (Q4_0, 6912, 1152, 8, GELU),
     (Q4_1, 100, 256, 1, GELU),      # hidden not a multiple of 16: padded group
     (Q4_1, 100, 256, 3, SILU),
-    (Q4_1, 100, 256, 20, GELU),     # tensor-core GEMM (80-byte rows), padded group
+    (Q4_1, 100, 256, 20, GELU),     # decode-batch GEMM (160-byte rows), padded group
     (Q8_0, 8, 64, 1, SILU),         # a single partial group
-    (Q4_0, 2048, 4096, 32, GELU),   # tensor-core GEMM, one token tile
-    (Q4_0, 2048, 4096, 200, SILU),  # tensor-core GEMM, two token tiles
+    (Q4_0, 2048, 4096, 32, GELU),   # decode-batch GEMM, 32-token tile
+    (Q4_0, 2048, 4096, 200, SILU),  # prefill GEMM, two token tiles
     (Q8_0, 1024, 16384, 1, GELU),   # 35.6 MB: the streaming GEMV
     (Q8_0, 1024, 16384, 9, SILU),
 ]

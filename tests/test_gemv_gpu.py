@@ -86,10 +86,19 @@ def assert_bits_equal(y, ref, msg=""):
 
 
 def gemm_path(dt, act, m, k):
-    """True when the library runs this call on the tensor-core GEMM: f32
-    activations, M >= 17 and a weight row pitch that is a multiple of 16 bytes
-    (qmm_kernels.cuh: gemm_supported)."""
-    return act == 0 and m >= 17 and ((k // 32) * BB[dt]) % 16 == 0
+    """True when the library runs this call on the prefill tensor-core GEMM
+    (f16 operands rounded once): f32 activations, M > 128 and a weight row
+    pitch that is a multiple of 16 bytes (qmm_kernels.cuh: gemm_supported).
+    Decode batches (17 <= M <= 128) run on the decode-batch GEMM, whose exact
+    operand split keeps the GEMV paths' accuracy."""
+    return act == 0 and m > 128 and ((k // 32) * BB[dt]) % 16 == 0
+
+
+def gemm_tn_path(dt, act, m, k, n):
+    """True for the decode-batch GEMM: f32 activations, 17 <= M <= 128, row
+    pitch 0 or 8 mod 16 bytes (N even for the latter)."""
+    rb = (k // 32) * BB[dt]
+    return act == 0 and 17 <= m <= 128 and (rb % 16 == 0 or (rb % 16 == 8 and n % 2 == 0))
 
 
 # The GEMM rounds both operands to f16 (unit roundoff 2^-11): the norm-wise
@@ -164,8 +173,18 @@ def test_config3_prefill_q4_0_gemm(oracle, torch_cuda, qlib):
 
 # Tensor-core GEMM shapes: ragged M (token tiles of 128), ragged N (weight
 # tiles of 128), K not a multiple of the 256-element raw chunk or the 64-element
-# K step (zero-filled boxes), all three block types.
+# K step (zero-filled boxes), all three block types. M <= 128 runs the
+# decode-batch GEMM (token tiles of 32 / 64 / 128 on the MMA's N side; row
+# pitches of 8 mod 16 through the paired-row view: K = 1152, 1408, 1088), the
+# rest the prefill GEMM.
 GEMM = [
+    (Q4_0, 24, 1152, 1536),   # Gemma QKV at batch 24: paired rows, K split
+    (Q8_0, 64, 1152, 2048),   # paired, 64-token tile
+    (Q4_0, 100, 6912, 1152),  # 128-token tile, K split
+    (Q8_0, 33, 1152, 262),    # paired, ragged N (even), 64-token tile
+    (Q4_0, 17, 1408, 200),    # paired, K = 5.5 raw chunks
+    (Q4_1, 40, 1088, 96),     # Q4_1 paired (34 blocks a row)
+    (Q8_0, 128, 4096, 640),   # the largest decode batch
     (Q4_0, 17, 256, 64),
     (Q4_0, 32, 8192, 200),
     (Q4_0, 129, 512, 1000),
@@ -183,7 +202,9 @@ def test_gemm_shapes(oracle, torch_cuda, qlib, case):
     dt, m, k, n = GEMM[case]
     w = make_weights(oracle, dt, n, k, seed=700 + case)
     x = np.random.default_rng(750 + case).normal(0, 1, m * k).astype(np.float32)
-    check(oracle, torch_cuda, qlib, dt, 0, x, w, m, k, n)
+    rel = check(oracle, torch_cuda, qlib, dt, 0, x, w, m, k, n)
+    if gemm_tn_path(dt, 0, m, k, n):
+        assert rel < 5e-5, rel  # exact operand split: ~1e-6 expected
     check(oracle, torch_cuda, qlib, dt, 1, x, w, m, k, n)  # Q8_0 activations: GEMV, bit-exact
 
 

@@ -154,7 +154,7 @@ int check_shape(int dt, size_t m, size_t k, size_t n, size_t w_len) {
 size_t workspace_for(int dt, int act, size_t m, size_t n, size_t k, int dev) {
     if (m == 0 || n == 0) return 0;
     if (gemm_supported(dt, act == QMM_ACT_Q8_0, (int)m, (int)n, (int)k))
-        return gemm_workspace_bytes((int)m, (int)n, (int)k, dt);
+        return gemm_workspace_bytes((int)m, (int)n, (int)k, dt, act == QMM_ACT_Q8_0);
     const size_t rows = m < kMaxGemvRows ? m : kMaxGemvRows;
     GemvPlan p;
     if (!gemv_plan(dt, act == QMM_ACT_Q8_0, (int)rows, (int)n, (int)k, num_sms(dev), &p)) return 0;
@@ -174,9 +174,10 @@ int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size
     int* err = device_error_word(dev);
     // prefill-sized M: one tensor-core GEMM over all rows
     if (gemm_supported(dt, act == QMM_ACT_Q8_0, (int)m, (int)n, (int)k)) {
-        if (gemm_workspace_bytes((int)m, (int)n, (int)k, dt) > ws_bytes)
+        const bool native = act == QMM_ACT_Q8_0;
+        if (gemm_workspace_bytes((int)m, (int)n, (int)k, dt, native) > ws_bytes)
             return fail(QMM_ERR_INVALID_INPUT, "workspace too small");
-        cudaError_t e = launch_gemm(dt, w, x, y, (int)m, (int)n, (int)k, ws, err, st, immutable_w, g);
+        cudaError_t e = launch_gemm(dt, w, x, y, (int)m, (int)n, (int)k, ws, err, st, immutable_w, g, native);
         if (e != cudaSuccess) return cuda_fail(e, "launch_gemm");
         return QMM_OK;
     }

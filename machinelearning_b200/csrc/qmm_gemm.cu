@@ -603,6 +603,7 @@ cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 // (qmm_gemm_tn.cu, exact operand split, 8-mod-16 row pitches too); larger M on
 // the prefill GEMM below.
 bool gemm_supported(int qt, bool native, int M, int N, int K) {
+    if (native) return gemm_i8_supported(qt, M, N, K);
     if (gemm_tn_supported(qt, native, M, N, K)) return true;
     if (native || M <= kGemmTnMaxRows || N < 1 || K < QK || K % QK) return false;
     const int bb = block_bytes(qt);
@@ -652,7 +653,8 @@ GemmPlan gemm_plan(int qt, int M, int N, int K) {
 size_t x16_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((size_t)M * 4); }
 }  // namespace
 
-size_t gemm_workspace_bytes(int M, int N, int K, int qt) {
+size_t gemm_workspace_bytes(int M, int N, int K, int qt, bool native) {
+    if (native) return gemm_i8_workspace_bytes(M, N, K, qt);
     if (gemm_tn_supported(qt, false, M, N, K)) return gemm_tn_workspace_bytes(M, N, K, qt);
     const GemmPlan p = gemm_plan(qt, M, N, K);
     size_t b = x16_bytes(M, K);
@@ -664,7 +666,8 @@ size_t gemm_workspace_bytes(int M, int N, int K, int qt) {
 }
 
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws, int* err,
-                        cudaStream_t st, bool weights_immutable, const GatedOut& g) {
+                        cudaStream_t st, bool weights_immutable, const GatedOut& g, bool native) {
+    if (native) return launch_gemm_i8(qt, w, x, y, M, N, K, ws, err, st, weights_immutable);
     if (gemm_tn_supported(qt, false, M, N, K))
         return launch_gemm_tn(qt, w, x, y, M, N, K, ws, err, st, weights_immutable, g);
     __half* x16 = static_cast<__half*>(ws);

@@ -628,7 +628,8 @@ size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
 int tn_nt(int M) { return M <= 32 ? 32 : (M <= 64 ? 64 : 128); }
 
 // Launch shape: K slices (1, 2, 4 or 8, whole raw chunks each) for the fewest
-// rounds of CTAs (one per SM) times K steps per CTA, with a 3% charge per
+// rounds of CTAs (one per SM) times (K steps per CTA + a CTA's fixed cost of
+// set-up, pipeline fill and epilogue, worth ~24 K steps), with a 3% charge per
 // split for the slab round trip.
 struct TnPlan {
     int nt, ks, cps;
@@ -647,7 +648,7 @@ TnPlan tn_plan(int M, int N, int K) {
         if ((nch + cps - 1) / cps != ks) continue;  // every slice gets a chunk
         const long rounds = (tiles * ks + sms - 1) / sms;
         const int steps = min(ksteps, cps * kTnStepsPerChunk);
-        const double cost = (double)rounds * (steps + 2.0) * (1.0 + 0.03 * (ks > 1 ? 1 : 0));
+        const double cost = (double)rounds * (steps + 24.0) * (1.0 + 0.03 * (ks > 1 ? 1 : 0));
         if (best < 0.0 || cost < best) {
             best = cost;
             p.ks = ks;

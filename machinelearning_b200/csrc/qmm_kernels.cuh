@@ -231,10 +231,12 @@ constexpr int kGemmMinRows = 17;
 bool gemm_supported(int qt, bool native, int M, int N, int K);
 // x16 activations and scales, plus K-slice partials and tickets when the call's
 // plan splits K (planned per device the same way at launch).
-size_t gemm_workspace_bytes(int M, int N, int K, int qt);
-// ws: gemm_workspace_bytes(M, N, K, qt) bytes, 256-byte aligned.
+// native: Q8_0-quantised activations (the integer GEMM of qmm_gemm_i8.cu).
+size_t gemm_workspace_bytes(int M, int N, int K, int qt, bool native = false);
+// ws: gemm_workspace_bytes(M, N, K, qt, native) bytes, 256-byte aligned.
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
-                        int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut());
+                        int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut(),
+                        bool native = false);
 
 // ---- decode-batch GEMM (qmm_gemm_tn.cu): tcgen05, weights on the MMA's M side,
 // tokens on its N side, exact hi/lo split of both operands (~1e-6 relative).
@@ -245,6 +247,19 @@ bool gemm_tn_supported(int qt, bool native, int M, int N, int K);
 size_t gemm_tn_workspace_bytes(int M, int N, int K, int qt);
 cudaError_t launch_gemm_tn(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
                            int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut());
+
+// ---- integer GEMM for the Q8_0-activation modes (qmm_gemm_i8.cu): tcgen05
+// kind::i8, one MMA per 32-element block, the reference's per-block float
+// sequence in the epilogue (bit-identical). M >= kGemmMinRows, row pitch 0
+// or 8 mod 16 bytes (N even for the latter).
+bool gemm_i8_supported(int qt, int M, int N, int K);
+size_t gemm_i8_workspace_bytes(int M, int N, int K, int qt);
+cudaError_t launch_gemm_i8(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,
+                           int* err, cudaStream_t st, bool weights_immutable);
+// Activation prep of the integer GEMM (qmm_quant.cu): xq [M][K] s8, xs / xc
+// [nbp][Mp] (see the kernel).
+cudaError_t launch_xprep_i8gemm(int qt, const float* x, int M, int K, int Mp, int8_t* xq, float* xs, uint32_t* xc,
+                                cudaStream_t st);
 
 int* device_error_word(int device);
 

@@ -319,6 +319,41 @@ __global__ void xprep_q8_kernel(const float* __restrict__ x, int M, int K, int M
     }
 }
 
+// Q8_0-activation mode for the integer tensor-core GEMM (qmm_gemm_i8.cu): each
+// (token, block) quantised exactly as the reference does before its integer
+// dots (quantize_q8_0 for Q8_0 weights, quantize_row_q8_0 for Q4 weights), laid
+// out for TMA:
+//   xq  [M][K] s8, row-major (the K-major B operand);
+//   xs  [nbp][Mp] f32 = f32(f16(scale)), block-major (a tile's tokens contiguous);
+//   xc  [nbp][Mp] 32-bit: Q4_0 the integer 0x4B400000 - 8 * qsum (added to a
+//       block dot it gives the float bits of 2^23 + 2^22 + (dot - 8 qsum): an
+//       exact int-to-float conversion by one subtraction); Q4_1 (float)qsum;
+//       Q8_0 unused.
+// Mp = M rounded up to 4 (16-byte rows), nbp = K/32 rounded up to 4.
+template <int QT>
+__global__ void xprep_i8gemm_kernel(const float* __restrict__ x, int M, int K, int Mp, int8_t* __restrict__ xq,
+                                    float* __restrict__ xs, uint32_t* __restrict__ xc) {
+    pdl_launch_dependents();
+    pdl_wait();  // x may be produced by the preceding kernel in the stream
+    const int lane = threadIdx.x & 31;
+    const int nb = K / QK;
+    const int64_t total = (int64_t)nb * M;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t idx = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); idx < total; idx += warps) {
+        const int m = (int)(idx / nb);
+        const int b = (int)(idx % nb);
+        const float v = x[(int64_t)m * K + (int64_t)b * QK + lane];
+        const Q8Block r = q8_block_lane(v, QT != kQ8_0);
+        xq[(int64_t)m * K + (int64_t)b * QK + lane] = (int8_t)r.q;
+        const int qsum = warp_sum_i(r.q);
+        if (lane == 0) {
+            xs[(int64_t)b * Mp + m] = r.d_rt;
+            if (QT == kQ4_0) xc[(int64_t)b * Mp + m] = 0x4B400000u - (uint32_t)(8 * qsum);
+            if (QT == kQ4_1) xc[(int64_t)b * Mp + m] = __float_as_uint((float)qsum);
+        }
+    }
+}
+
 }  // namespace
 
 // ---- launchers ---------------------------------------------------------------------
@@ -421,6 +456,17 @@ cudaError_t launch_xprep_q8(int qt, const float* x, int M, int K, uint8_t* xq, u
 
 cudaError_t launch_pdl_kernel(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
     return launch_pdl(fn, grid, block, smem, st, args);
+}
+
+cudaError_t launch_xprep_i8gemm(int qt, const float* x, int M, int K, int Mp, int8_t* xq, float* xs, uint32_t* xc,
+                                cudaStream_t st) {
+    const int64_t total = (int64_t)(K / QK) * M;
+    const int grid = grid_for_warps(total, 8);
+    void* args[] = {(void*)&x, (void*)&M, (void*)&K, (void*)&Mp, (void*)&xq, (void*)&xs, (void*)&xc};
+    const void* fn = qt == kQ8_0 ? (const void*)xprep_i8gemm_kernel<kQ8_0>
+                                 : (qt == kQ4_0 ? (const void*)xprep_i8gemm_kernel<kQ4_0>
+                                                : (const void*)xprep_i8gemm_kernel<kQ4_1>);
+    return launch_pdl_kernel(fn, dim3(grid), dim3(256), 0, st, args);
 }
 
 }  // namespace qmm

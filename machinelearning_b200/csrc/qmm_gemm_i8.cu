@@ -32,11 +32,10 @@
 //   warps 6-13 the float epilogue: per block, tcgen05.ld of the int32 dots, an
 //              exact int-to-float conversion by the 2^23 + 2^22 magic number
 //              (Q4_0: the -8 * qsum correction pre-added by the activation
-//              prep), then the reference's multiplies and add in f32 pairs
-//              (mul/add.rn.f32x2: IEEE round-to-nearest per element, no
-//              contraction); two warps per TMEM lane quarter, each half of the
-//              tokens. Results are staged in shared memory and stored as whole
-//              rows.
+//              prep), then the reference's multiplies and add, each rounded on
+//              its own (no contraction into an fma); two warps per TMEM lane
+//              quarter, each half of the tokens. Results are staged in shared
+//              memory and stored as whole rows.
 // Every wait is bounded (the error word records a timeout; copies in flight
 // land before a CTA exits).
 #include <cuda.h>
@@ -130,7 +129,7 @@ __device__ __forceinline__ void tmem_ld_cols<32>(uint32_t taddr, uint32_t (&r)[3
     tmem_ld32(taddr, r);
 }
 
-// ---- f32 pairs (IEEE round to nearest per element; no contraction) ------------------
+// ---- f32 pairs (IEEE round to nearest per element) ---------------------------------
 __device__ __forceinline__ uint64_t pk(float a, float b) {
     return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
 }
@@ -138,11 +137,6 @@ __device__ __forceinline__ uint64_t pk_u(uint32_t a, uint32_t b) { return (uint6
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
     uint64_t r;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
 __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
@@ -394,9 +388,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
         const int half = (warp - 6) >> 2;     // which half of the token columns
         const int j = q * 32 + lane;          // tile row
         const int c0 = half * CH;             // first token column of this warp
-        uint64_t acc[CH / 2];
+        float acc[CH];
 #pragma unroll
-        for (int c = 0; c < CH / 2; ++c) acc[c] = 0ull;  // +0.0f pairs, the reference's `let mut dot = 0.0`
+        for (int c = 0; c < CH; ++c) acc[c] = 0.0f;  // the reference's `let mut dot = 0.0`
         pdl_wait();
         bool ok = true;
         for (int i = 0; i < steps && ok; ++i) {
@@ -416,18 +410,22 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
                 uint32_t v[CH];
                 tmem_ld_cols<CH>(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((tb * kI8Blocks + b) * NT + c0), v);
                 const float wsj = ws[b * kI8Rows + j];
-                const uint64_t w2 = pk(wsj, wsj);
                 const float* xs = xsb + b * NT + c0;
                 const uint32_t* xc = xcb + b * NT + c0;
+                // The conversion and the first product run on f32 pairs (exact, or
+                // a single rounding with no add to fuse with); the last product and
+                // the accumulation are scalar __fmul_rn / __fadd_rn, which the
+                // compiler never contracts into an fma.
                 if constexpr (QT == kQ4_1) {
                     const float wmj = ws[kI8Blocks * kI8Rows + b * kI8Rows + j];
-                    const uint64_t m2 = pk(wmj, wmj);
 #pragma unroll
                     for (int c = 0; c < CH; c += 2) {
                         const uint64_t fu = sub2(pk_u(v[c] + kMagicBits, v[c + 1] + kMagicBits), pk(kMagic, kMagic));
-                        const uint64_t qs = *reinterpret_cast<const uint64_t*>(xc + c);
-                        const uint64_t inner = add2(mul2(w2, fu), mul2(m2, qs));
-                        acc[c / 2] = add2(acc[c / 2], mul2(*reinterpret_cast<const uint64_t*>(xs + c), inner));
+                        const float f0 = __uint_as_float((uint32_t)fu), f1 = __uint_as_float((uint32_t)(fu >> 32));
+                        const float s0 = __fadd_rn(__fmul_rn(wsj, f0), __fmul_rn(wmj, __uint_as_float(xc[c])));
+                        const float s1 = __fadd_rn(__fmul_rn(wsj, f1), __fmul_rn(wmj, __uint_as_float(xc[c + 1])));
+                        acc[c] = __fadd_rn(acc[c], __fmul_rn(xs[c], s0));
+                        acc[c + 1] = __fadd_rn(acc[c + 1], __fmul_rn(xs[c + 1], s1));
                     }
                 } else {
 #pragma unroll
@@ -438,8 +436,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
                             k1 = xc[c + 1];
                         }
                         const uint64_t f = sub2(pk_u(v[c] + k0, v[c + 1] + k1), pk(kMagic, kMagic));
-                        const uint64_t t = mul2(mul2(f, *reinterpret_cast<const uint64_t*>(xs + c)), w2);
-                        acc[c / 2] = add2(acc[c / 2], t);
+                        const uint64_t t = mul2(f, *reinterpret_cast<const uint64_t*>(xs + c));
+                        acc[c] = __fadd_rn(acc[c], __fmul_rn(__uint_as_float((uint32_t)t), wsj));
+                        acc[c + 1] = __fadd_rn(acc[c + 1], __fmul_rn(__uint_as_float((uint32_t)(t >> 32)), wsj));
                     }
                 }
             }
@@ -456,10 +455,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
         float* ys = reinterpret_cast<float*>(sA);
         const int wr = i8_tile_row<PAIRED>(j);
 #pragma unroll
-        for (int c = 0; c < CH; c += 2) {
-            ys[(c0 + c) * YP + wr] = __uint_as_float((uint32_t)acc[c / 2]);
-            ys[(c0 + c + 1) * YP + wr] = __uint_as_float((uint32_t)(acc[c / 2] >> 32));
-        }
+        for (int c = 0; c < CH; ++c) ys[(c0 + c) * YP + wr] = acc[c];
         asm volatile("bar.sync 1, %0;" ::"r"(kI8EpiThreads) : "memory");
         const int et = threadIdx.x - 6 * 32;
         const int mv = min(NT, a.M - m0);

@@ -599,17 +599,27 @@ cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 
 }  // namespace
 
-// Routing: decode batches (M <= kGemmTnMaxRows) run on the decode-batch GEMM
-// (qmm_gemm_tn.cu, exact operand split, 8-mod-16 row pitches too); larger M on
+namespace {
+// Shapes the prefill GEMM below can run: 2-D TMA boxes of the raw rows need a
+// row pitch that is a multiple of 16 bytes.
+bool single_shape_ok(int qt, int M, int N, int K) {
+    if (M < kGemmMinRows || N < 1 || K < QK || K % QK) return false;
+    const int bb = block_bytes(qt);
+    return bb && ((int64_t)(K / QK) * bb) % 16 == 0;
+}
+// Decode batches of 33..kGemmTnMaxRows tokens run on the decode-batch GEMM
+// (qmm_gemm_tn.cu, exact operand split, 8-mod-16 row pitches too), and so do
+// 17..32 tokens where the prefill GEMM cannot take the row pitch; the rest on
 // the prefill GEMM below.
+bool route_tn(int qt, int M, int N, int K) {
+    if (!gemm_tn_supported(qt, false, M, N, K)) return false;
+    return M > kGemmSingleMaxRows || !single_shape_ok(qt, M, N, K);
+}
+}  // namespace
+
 bool gemm_supported(int qt, bool native, int M, int N, int K) {
     if (native) return gemm_i8_supported(qt, M, N, K);
-    if (gemm_tn_supported(qt, native, M, N, K)) return true;
-    if (native || M <= kGemmTnMaxRows || N < 1 || K < QK || K % QK) return false;
-    const int bb = block_bytes(qt);
-    if (!bb) return false;
-    const int64_t row_bytes = (int64_t)(K / QK) * bb;
-    return row_bytes % 16 == 0;  // 2-D TMA boxes of the raw rows
+    return route_tn(qt, M, N, K) || single_shape_ok(qt, M, N, K);
 }
 
 namespace {
@@ -655,7 +665,7 @@ size_t x16_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((
 
 size_t gemm_workspace_bytes(int M, int N, int K, int qt, bool native) {
     if (native) return gemm_i8_workspace_bytes(M, N, K, qt);
-    if (gemm_tn_supported(qt, false, M, N, K)) return gemm_tn_workspace_bytes(M, N, K, qt);
+    if (route_tn(qt, M, N, K)) return gemm_tn_workspace_bytes(M, N, K, qt);
     const GemmPlan p = gemm_plan(qt, M, N, K);
     size_t b = x16_bytes(M, K);
     if (p.ks > 1) {
@@ -668,7 +678,7 @@ size_t gemm_workspace_bytes(int M, int N, int K, int qt, bool native) {
 cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws, int* err,
                         cudaStream_t st, bool weights_immutable, const GatedOut& g, bool native) {
     if (native) return launch_gemm_i8(qt, w, x, y, M, N, K, ws, err, st, weights_immutable);
-    if (gemm_tn_supported(qt, false, M, N, K))
+    if (route_tn(qt, M, N, K))
         return launch_gemm_tn(qt, w, x, y, M, N, K, ws, err, st, weights_immutable, g);
     __half* x16 = static_cast<__half*>(ws);
     float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256((size_t)M * K * 2));

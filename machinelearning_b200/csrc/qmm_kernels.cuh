@@ -241,8 +241,14 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
 // ---- decode-batch GEMM (qmm_gemm_tn.cu): tcgen05, weights on the MMA's M side,
 // tokens on its N side, exact hi/lo split of both operands (~1e-6 relative).
 // f32-activation calls with kGemmMinRows <= M <= kGemmTnMaxRows and a row
-// pitch of 0 or 8 mod 16 bytes (N even for the latter).
+// pitch of 0 or 8 mod 16 bytes (N even for the latter). Calls of at most
+// kGemmSingleMaxRows tokens whose pitch is a multiple of 16 bytes run on the
+// prefill GEMM instead: its single f16 rounding (~3e-4 norm-wise, inside the
+// 1e-3 contract) costs one MMA per K slice where the exact split costs a
+// double-width one, and at 32 tokens the split's fixed per-step cost doubles
+// the call (Llama-70B gate at 32 tokens on B200: 73 us against 164 us).
 constexpr int kGemmTnMaxRows = 128;
+constexpr int kGemmSingleMaxRows = 32;
 bool gemm_tn_supported(int qt, bool native, int M, int N, int K);
 size_t gemm_tn_workspace_bytes(int M, int N, int K, int qt);
 cudaError_t launch_gemm_tn(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,

@@ -91,11 +91,11 @@ def _quant_weight(dt: int, n: int, k: int, data, device: int, kpad: int = 0) -> 
 
 def padded_k(k: int, batch: int) -> int:
     """Columns a batch-matmul weight of k columns is padded to. Batches of 17
-    to 128 run on the decode-batch tensor-core GEMM, which reads row pitches
-    of 0 or 8 mod 16 bytes in place (Q4_0 / Q8_0 rows are 18 / 34 bytes per 32
-    columns: k/32 a multiple of 4); larger batches run on the prefill GEMM,
-    which needs a 16-byte pitch (k/32 a multiple of 8); smaller batches keep
-    k (GEMV)."""
+    to 128 run on the tensor-core GEMMs; the decode-batch GEMM reads row
+    pitches of 0 or 8 mod 16 bytes in place (Q4_0 / Q8_0 rows are 18 / 34
+    bytes per 32 columns: k/32 a multiple of 4); larger batches run on the
+    prefill GEMM, which needs a 16-byte pitch (k/32 a multiple of 8) and also
+    takes 17..32 tokens where the pitch allows; smaller batches keep k (GEMV)."""
     nb = k // 32
     if batch < 17 or nb % 8 == 0 or (batch <= 128 and nb % 4 == 0):
         return k

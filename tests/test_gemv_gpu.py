@@ -87,18 +87,21 @@ def assert_bits_equal(y, ref, msg=""):
 
 def gemm_path(dt, act, m, k):
     """True when the library runs this call on the prefill tensor-core GEMM
-    (f16 operands rounded once): f32 activations, M > 128 and a weight row
-    pitch that is a multiple of 16 bytes (qmm_kernels.cuh: gemm_supported).
-    Decode batches (17 <= M <= 128) run on the decode-batch GEMM, whose exact
+    (f16 operands rounded once): f32 activations, M > 128 or 17 <= M <= 32,
+    and a weight row pitch that is a multiple of 16 bytes (qmm_gemm.cu:
+    route_tn, single_shape_ok). Decode batches of 33..128 tokens, and 17..32
+    tokens whose pitch is 8 mod 16, run on the decode-batch GEMM, whose exact
     operand split keeps the GEMV paths' accuracy."""
-    return act == 0 and m > 128 and ((k // 32) * BB[dt]) % 16 == 0
+    return act == 0 and (m > 128 or 17 <= m <= 32) and ((k // 32) * BB[dt]) % 16 == 0
 
 
 def gemm_tn_path(dt, act, m, k, n):
     """True for the decode-batch GEMM: f32 activations, 17 <= M <= 128, row
-    pitch 0 or 8 mod 16 bytes (N even for the latter)."""
+    pitch 0 or 8 mod 16 bytes (N even for the latter), and not taken by the
+    prefill GEMM."""
     rb = (k // 32) * BB[dt]
-    return act == 0 and 17 <= m <= 128 and (rb % 16 == 0 or (rb % 16 == 8 and n % 2 == 0))
+    tn = act == 0 and 17 <= m <= 128 and (rb % 16 == 0 or (rb % 16 == 8 and n % 2 == 0))
+    return tn and not gemm_path(dt, act, m, k)
 
 
 # The GEMM rounds both operands to f16 (unit roundoff 2^-11): the norm-wise
@@ -173,10 +176,10 @@ def test_config3_prefill_q4_0_gemm(oracle, torch_cuda, qlib):
 
 # Tensor-core GEMM shapes: ragged M (token tiles of 128), ragged N (weight
 # tiles of 128), K not a multiple of the 256-element raw chunk or the 64-element
-# K step (zero-filled boxes), all three block types. M <= 128 runs the
-# decode-batch GEMM (token tiles of 32 / 64 / 128 on the MMA's N side; row
-# pitches of 8 mod 16 through the paired-row view: K = 1152, 1408, 1088), the
-# rest the prefill GEMM.
+# K step (zero-filled boxes), all three block types. 33 <= M <= 128, and
+# 17..32 with a pitch of 8 mod 16, run the decode-batch GEMM (row pitches of 8
+# mod 16 through the paired-row view: K = 1152, 1408, 1088), the rest the
+# prefill GEMM.
 GEMM = [
     (Q4_0, 24, 1152, 1536),   # Gemma QKV at batch 24: paired rows, K split
     (Q8_0, 64, 1152, 2048),   # paired, 64-token tile

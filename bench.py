@@ -82,6 +82,14 @@ WORKLOADS = {
         projections=[("gate", 8192, 28672, Q4_0, "col"), ("up", 8192, 28672, Q4_0, "col"),
                      ("down", 28672, 8192, Q4_0, "row"), ("lm_head", 8192, 128256, Q8_0, "col")],
         batches=[1, 32], copies=1, model="Llama-3-70B layer set"),
+    # the same layer set with Megatron pairing: gate/up column shards fused
+    # (SwiGLU epilogue) feed the row-parallel down directly, so N > 1 needs no
+    # all-gather between them; bytes are counted as the four reference GEMVs
+    "llama70b-megatron": dict(
+        config_index=4,
+        projections=[("gate+up", 8192, 28672, Q4_0, "gated"), ("down", 28672, 8192, Q4_0, "row_h"),
+                     ("lm_head", 8192, 128256, Q8_0, "col")],
+        batches=[1, 32], copies=1, model="Llama-3-70B layer set, Megatron-paired FFN (gate/up -> SwiGLU -> down)"),
     "llama70b-gate": dict(
         config_index=4, projections=[("gate", 8192, 28672, Q4_0, "col")], batches=[1], copies=2,
         model="Llama-3-70B FFN gate, Q4_0"),
@@ -114,6 +122,23 @@ def work(wl, m, k, n, dt):
 
 def alg_bytes(m, k, n, dt):
     return m * k * 4 + n * (k // 32) * BB[dt] + m * n * 4
+
+
+def gemvs_of(kind):
+    """Reference GEMVs one projection stands for (a fused gate/up is two)."""
+    return 2 if kind == "gated" else 1
+
+
+def reference_gemvs(wl):
+    """The workload as the reference's independent GEMVs (a fused gate/up pair
+    as its gate and up matmuls): what the CPU baseline times."""
+    out = []
+    for name, k, n, dt, kind in wl["projections"]:
+        if kind == "gated":
+            out += [("gate", k, n, dt, "col"), ("up", k, n, dt, "col")]
+        else:
+            out.append((name, k, n, dt, "row" if kind == "row_h" else kind))
+    return out
 
 
 def host_cores():
@@ -251,7 +276,10 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from machinelearning_b200 import _lib
+    from machinelearning_b200._lib import SILU
+    from machinelearning_b200.fused import fuse_gate_up
     from machinelearning_b200.linear import QuantWeight
+    from machinelearning_b200.tp import TpComm
 
     L = _lib.lib()
     wl = WORKLOADS[args.workload]
@@ -260,64 +288,80 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream(dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
     copies = args.copies or wl["copies"]
+    # N > 1: the library's own NCCL communicator (include/qmm_tp.h), non-blocking, bounded waits
+    comm = TpComm.from_group(local_rank, timeout_s=120.0) if world > 1 else None
 
     # ---- weights: this rank's shard of every projection, `copies` layers --------------
-    # column-parallel: rows [r*N/W, (r+1)*N/W); row-parallel: blocks [r*nb/W, (r+1)*nb/W) of every row
+    # column-parallel (col, gated): rows [r*N/W, (r+1)*N/W); row-parallel (row,
+    # row_h): blocks [r*nb/W, (r+1)*nb/W) of every row
     problems = []  # (name, k_local, n_local, dt, kind, k_full, n_full)
     for name, k, n, dt, kind in wl["projections"]:
-        if world > 1 and kind == "col":
-            assert n % world == 0, f"{name}: N={n} not divisible by {world}"
+        if kind in ("col", "gated"):
+            assert n % world == 0 and (kind == "col" or (n // world) % 32 == 0), f"{name}: N={n} over {world}"
             problems.append((name, k, n // world, dt, kind, k, n))
-        elif world > 1 and kind == "row":
+        else:
             assert (k // 32) % world == 0, f"{name}: K={k} blocks not divisible by {world}"
             problems.append((name, k // world, n, dt, kind, k, n))
-        else:
-            problems.append((name, k, n, dt, kind, k, n))
 
     gen = torch.Generator(device=dev)
-    weights = []  # [copy][problem] -> QuantWeight
+
+    def make_weight(seed, dt, nl, kl):
+        gen.manual_seed(seed)
+        wf = torch.randn(nl * kl, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        qb = torch.empty(nl * (kl // 32) * BB[dt], dtype=torch.uint8, device=dev)
+        _lib.check(L.qmm_quantize_dev(dt, 0, wf.data_ptr(), wf.numel(), qb.data_ptr(), None, sp))
+        stream.synchronize()
+        return QuantWeight.from_device(dt, nl, kl, qb)
+
+    weights = []  # [copy][problem] -> QuantWeight (a gate/up pair: the fused weight)
     with torch.cuda.stream(stream):
         for c in range(copies):
             row = []
             for pi, (name, kl, nl, dt, kind, k, n) in enumerate(problems):
-                gen.manual_seed(1000 * c + 17 * pi + 1 + rank * 7919)
-                wf = torch.randn(nl * kl, generator=gen, device=dev, dtype=torch.float32) * 0.02
-                qb = torch.empty(nl * (kl // 32) * BB[dt], dtype=torch.uint8, device=dev)
-                _lib.check(L.qmm_quantize_dev(dt, 0, wf.data_ptr(), wf.numel(), qb.data_ptr(), None, sp))
-                stream.synchronize()
-                row.append(QuantWeight.from_device(dt, nl, kl, qb))
-                del wf, qb
+                seed = 1000 * c + 17 * pi + 1 + rank * 7919
+                if kind == "gated":
+                    g, u = make_weight(seed, dt, nl, kl), make_weight(seed + 500, dt, nl, kl)
+                    row.append(fuse_gate_up(g, u))
+                    g.close()
+                    u.close()
+                else:
+                    row.append(make_weight(seed, dt, nl, kl))
             weights.append(row)
     torch.cuda.synchronize(dev)
 
     # ---- activations / outputs per (batch, problem) -----------------------------------
-    xs, ys, gathered = {}, {}, {}
+    # a row_h projection reads the preceding gated projection's hidden slice
+    xs, ys = {}, {}
     for b in wl["batches"]:
         for pi, (name, kl, nl, dt, kind, k, n) in enumerate(problems):
             gen.manual_seed(50000 + 31 * pi + b)
-            xs[(b, pi)] = torch.randn(b, kl, generator=gen, device=dev, dtype=torch.float32)
-            ys[(b, pi)] = torch.empty(b, nl, device=dev, dtype=torch.float32)
-            if world > 1 and kind == "col":
-                gathered[(b, pi)] = torch.empty(world * b * nl, device=dev, dtype=torch.float32)
+            xs[(b, pi)] = (ys[(b, pi - 1)] if kind == "row_h" else
+                           torch.randn(b, kl, generator=gen, device=dev, dtype=torch.float32))
+            ys[(b, pi)] = torch.empty(b, nl * (world if kind == "col" else 1), device=dev, dtype=torch.float32)
 
     # the library's per-stream workspace must exist before graph capture
-    need = max(L.qmm_workspace_size(dt, 0, b, nl, kl) for b in wl["batches"] for (_, kl, nl, dt, *_r) in problems)
+    need = max(L.qmm_workspace_size(dt, 0, b, nl * gemvs_of(kind), kl) for b in wl["batches"]
+               for (_, kl, nl, dt, kind, *_r) in problems)
     _lib.check(L.qmm_reserve_workspace(local_rank, sp, need + (1 << 20)))
 
     def one_step(c):
         for b in wl["batches"]:
             for pi, (name, kl, nl, dt, kind, k, n) in enumerate(problems):
-                x, y = xs[(b, pi)], ys[(b, pi)]
-                _lib.check(L.qmm_linear_forward(weights[c][pi].handle, x.data_ptr(), b, y.data_ptr(), 0, sp))
-                if world > 1:
-                    if kind == "col":
-                        dist.all_gather_into_tensor(gathered[(b, pi)], y.view(-1))
-                    else:
-                        dist.all_reduce(y)
+                w, x, y = weights[c][pi].handle, xs[(b, pi)].data_ptr(), ys[(b, pi)].data_ptr()
+                if kind == "gated":
+                    _lib.check(L.qmm_gated_forward(w, x, b, y, SILU, sp))
+                elif comm is None:
+                    _lib.check(L.qmm_linear_forward(w, x, b, y, 0, sp))
+                elif kind == "col":
+                    _lib.check(L.qmm_tp_column_forward(comm.handle, w, x, b, y, 0, sp))
+                else:
+                    _lib.check(L.qmm_tp_row_forward(comm.handle, w, x, b, y, 0, sp))
 
     launches_per_step = None  # counted by the library while one step is captured
-    steps_bytes = sum(alg_bytes(b, k, n, dt) for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems)
-    steps_work = sum(work(wl, b, k, n, dt) for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems)
+    steps_bytes = sum(gemvs_of(kind) * alg_bytes(b, k, n, dt) for b in wl["batches"]
+                      for (_, kl, nl, dt, kind, k, n) in problems)
+    steps_work = sum(gemvs_of(kind) * work(wl, b, k, n, dt) for b in wl["batches"]
+                     for (_, kl, nl, dt, kind, k, n) in problems)
     metric, unit, div = metric_info(wl)
 
     # ---- CUDA graphs ---------------------------------------------------------------------
@@ -374,7 +418,8 @@ def run_ours(args, rank, world, local_rank):
     value = steps_work * args.steps / (ms / 1e3) / div
 
     # ---- end to end through the C ABI with host buffers ------------------------------------
-    e2e = None if args.no_e2e else run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies)
+    e2e = None if args.no_e2e else run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies,
+                                                 comm)
 
     # ---- CPU baseline (rank 0, N=1): the reference path restated in oracle/ -----------------
     cpu = None
@@ -384,8 +429,11 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = load_peaks(tensor=wl.get("metric") == "flops")
     clocks = sampler.summary()
     clocks["samples_in_timed_region"] = n_timed
-    # graphs that hold NCCL calls are released before the process group goes
+    # graphs that hold NCCL calls are released before the communicator goes
     graphs.clear()
+    if comm is not None:
+        stream.synchronize()
+        _lib.check(comm.close())
     line = None
     if rank == 0:
         line = {
@@ -407,12 +455,15 @@ def run_ours(args, rank, world, local_rank):
                 "workload": args.workload,
                 "baseline_config_index": wl["config_index"],
                 "model": wl["model"],
-                "projections": [f"{p[0]} {p[5]}->{p[6]} {'Q8_0' if p[3] == Q8_0 else 'Q4_0'}" for p in problems],
+                "projections": [f"{p[0]} {p[5]}->{p[6]}{' x2 (fused, SwiGLU epilogue)' if p[4] == 'gated' else ''} "
+                                f"{'Q8_0' if p[3] == Q8_0 else 'Q4_0'} {p[4]}" for p in problems],
                 "batches": wl["batches"],
-                "parallelism": f"tp{world}" if world > 1 else "single",
+                "parallelism": (f"tp{world} (libqmm NCCL communicator: column-parallel all-gather, row-parallel "
+                                f"all-reduce)" if world > 1 else "single"),
                 "l2": f"{copies} weight copies rotated" + (" (>L2)" if copies > 1 else "; weights > L2"),
                 "algorithmic_bytes_per_step": steps_bytes,
-                "algorithmic_flops_per_step": sum(2 * b * k * n for b in wl["batches"] for (_, kl, nl, dt, kind, k, n) in problems),
+                "algorithmic_flops_per_step": sum(2 * gemvs_of(kind) * b * k * n for b in wl["batches"]
+                                                  for (_, kl, nl, dt, kind, k, n) in problems),
                 "graph": "one CUDA graph per pass over the weight copies plus one for the remaining K % copies steps; "
                          "PDL between kernels",
             },
@@ -438,21 +489,20 @@ def run_ours(args, rank, world, local_rank):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-    del weights, xs, ys, gathered
+    del weights, xs, ys
     torch.cuda.empty_cache()
     return line
 
 
-def run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies):
+def run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies, comm):
     """Same metric through the host-buffer C-ABI entry point: every call copies
     x in from pinned host memory, runs the GEMV and copies y out (synchronous),
     as a drop-in Linear::forward with host tensors would."""
     import torch
-    import torch.distributed as dist
     from machinelearning_b200 import _lib
 
-    if world > 1:
-        return e2e_tp(args, wl, problems, weights, L, sp, stream, world, dev, copies)
+    if world > 1 or any(p[4] in ("gated", "row_h") for p in problems):
+        return e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, comm)
     hx, hy = {}, {}
     h2d = d2h = 0
     for b in wl["batches"]:
@@ -482,57 +532,75 @@ def run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies):
             "path": "qmm_linear_forward_host (C ABI, pinned host x/y, one synchronous call per GEMV)"}
 
 
-def e2e_tp(args, wl, problems, weights, L, sp, stream, world, dev, copies):
+def e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, comm):
+    """Pinned host x -> device -> the library's forward (the tensor-parallel C
+    ABI for N > 1) -> pinned host y, every projection, one synchronize per step;
+    a Megatron-paired FFN copies in x and copies out down's y only."""
     import torch
     import torch.distributed as dist
     from machinelearning_b200 import _lib
+    from machinelearning_b200._lib import SILU
 
-    hx, hy, dx, dy, gat = {}, {}, {}, {}, {}
+    hx, hy, dx, dy = {}, {}, {}, {}
     h2d = d2h = 0
     for b in wl["batches"]:
         for pi, (name, kl, nl, dt, kind, k, n) in enumerate(problems):
-            hx[(b, pi)] = torch.randn(b, kl).pin_memory()
-            dx[(b, pi)] = torch.empty(b, kl, device=dev)
-            dy[(b, pi)] = torch.empty(b, nl, device=dev)
             out_n = nl * world if kind == "col" else nl
-            hy[(b, pi)] = torch.empty(b * out_n).pin_memory()
-            if kind == "col":
-                gat[(b, pi)] = torch.empty(b * out_n, device=dev)
-            h2d += b * kl * 4
-            d2h += b * out_n * 4
+            dy[(b, pi)] = torch.empty(b, out_n, device=dev)
+            if kind == "row_h":
+                dx[(b, pi)] = dy[(b, pi - 1)]
+            else:
+                hx[(b, pi)] = torch.randn(b, kl).pin_memory()
+                dx[(b, pi)] = torch.empty(b, kl, device=dev)
+                h2d += b * kl * 4
+            if kind != "gated":
+                hy[(b, pi)] = torch.empty(b, out_n).pin_memory()
+                d2h += b * out_n * 4
     steps = max(3, min(args.steps, 100))
 
     def step(c):
         with torch.cuda.stream(stream):
             for b in wl["batches"]:
                 for pi, (name, kl, nl, dt, kind, k, n) in enumerate(problems):
-                    dx[(b, pi)].copy_(hx[(b, pi)], non_blocking=True)
-                    _lib.check(L.qmm_linear_forward(weights[c][pi].handle, dx[(b, pi)].data_ptr(), b,
-                                                    dy[(b, pi)].data_ptr(), 0, sp))
-                    if kind == "col":
-                        dist.all_gather_into_tensor(gat[(b, pi)], dy[(b, pi)].view(-1))
-                        hy[(b, pi)].copy_(gat[(b, pi)], non_blocking=True)
+                    if (b, pi) in hx:
+                        dx[(b, pi)].copy_(hx[(b, pi)], non_blocking=True)
+                    w, x, y = weights[c][pi].handle, dx[(b, pi)].data_ptr(), dy[(b, pi)].data_ptr()
+                    if kind == "gated":
+                        _lib.check(L.qmm_gated_forward(w, x, b, y, SILU, sp))
+                    elif comm is None:
+                        _lib.check(L.qmm_linear_forward(w, x, b, y, 0, sp))
+                    elif kind == "col":
+                        _lib.check(L.qmm_tp_column_forward(comm.handle, w, x, b, y, 0, sp))
                     else:
-                        dist.all_reduce(dy[(b, pi)])
-                        hy[(b, pi)].copy_(dy[(b, pi)].view(-1), non_blocking=True)
-            stream.synchronize()
+                        _lib.check(L.qmm_tp_row_forward(comm.handle, w, x, b, y, 0, sp))
+                    if (b, pi) in hy:
+                        hy[(b, pi)].copy_(dy[(b, pi)], non_blocking=True)
+            if comm is not None:
+                _lib.check(comm.wait(120.0))
+            else:
+                stream.synchronize()
 
     for i in range(3):
         step(i % copies)
-    dist.barrier()
+    if world > 1:
+        dist.barrier()
     t0 = time.perf_counter()
     for i in range(steps):
         step(i % copies)
-    dist.barrier()
+    if world > 1:
+        dist.barrier()
     dt_s = time.perf_counter() - t0
-    t = torch.tensor([dt_s], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dt_s = float(t.item())
-    work_step = sum(work(wl, b, k, n, d) for b in wl["batches"] for (_, kl, nl, d, kind, k, n) in problems)
+    if world > 1:
+        t = torch.tensor([dt_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt_s = float(t.item())
+    work_step = sum(gemvs_of(kind) * work(wl, b, k, n, d) for b in wl["batches"]
+                    for (_, kl, nl, d, kind, k, n) in problems)
     _, unit, div = metric_info(wl)
     return {"value": round(work_step * steps / dt_s / div, 1), "unit": unit, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(dt_s * 1e3 / steps, 4),
-            "path": "pinned host x -> qmm_linear_forward on the shard -> NCCL join -> pinned host y, per GEMV"}
+            "path": ("pinned host x -> the library's forward on this rank's shard (qmm_tp_* NCCL join for N > 1) -> "
+                     "pinned host y, one wait per step")}
 
 
 # ---- CPU: the reference path restated (oracle/) -------------------------------------------
@@ -548,7 +616,7 @@ def cpu_setup(wl, max_rows_frac=1.0, layers=None):
     ws = []
     for c in range(layers):
         row = []
-        for name, k, n, dt, kind in wl["projections"]:
+        for name, k, n, dt, kind in reference_gemvs(wl):
             rows = max(32, int(n * max_rows_frac))
             rows = min(rows, n)
             nb = k // 32
@@ -558,14 +626,14 @@ def cpu_setup(wl, max_rows_frac=1.0, layers=None):
             row.append((raw.ravel(), rows))
         ws.append(row)
     xs = {(b, i): rng.normal(0, 1, b * p[1]).astype(np.float32)
-          for b in wl["batches"] for i, p in enumerate(wl["projections"])}
+          for b in wl["batches"] for i, p in enumerate(reference_gemvs(wl))}
     return oracle, ws, xs
 
 
 def cpu_step(oracle, wl, ws, xs, c):
     bytes_done = 0
     for b in wl["batches"]:
-        for i, (name, k, n, dt, kind) in enumerate(wl["projections"]):
+        for i, (name, k, n, dt, kind) in enumerate(reference_gemvs(wl)):
             w, rows = ws[c][i]
             fn = oracle.matmul_f32_q8 if dt == Q8_0 else oracle.matmul_f32_q4
             fn(xs[(b, i)], w, b, k, rows)
@@ -833,7 +901,8 @@ def run_decode_reference(args, rank, world):
 
 DEFAULT_WORKLOAD = "llama70b"  # the configuration defined at 1/2/4/8 GPUs
 # the other BASELINE configurations, timed in the same default run (one GPU)
-SUB_WORKLOADS = [("gemma-q8-sweep", None), ("q4-gemv", None), ("prefill", None), ("gemma-decode", 1),
+SUB_WORKLOADS = [("llama70b-megatron", None), ("gemma-q8-sweep", None), ("q4-gemv", None), ("prefill", None),
+                 ("gemma-decode", 1),
                  ("gemma-decode", 16), ("gemma-decode", 64)]
 
 
@@ -889,11 +958,12 @@ def main(argv=None):
     _init_dist(world, local_rank)
     try:
         line = _run_one(args, rank, world, local_rank)
-        if default_run and world == 1 and not args.no_sub:
-            # every other BASELINE configuration, timed in this same run
+        if default_run and not args.no_sub:
+            # every other BASELINE configuration, timed in this same run (one
+            # GPU); with N GPUs the Megatron-paired form of the same layer set
             subs = {}
             shared = None
-            for name, batch in SUB_WORKLOADS:
+            for name, batch in (SUB_WORKLOADS if world == 1 else [("llama70b-megatron", None)]):
                 sub = argparse.Namespace(**vars(args))
                 sub.workload, sub.copies = name, None
                 if batch is not None:

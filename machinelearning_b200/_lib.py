@@ -1,4 +1,5 @@
-"""ctypes binding of libqmm.so (the C ABI declared in include/qmm.h).
+"""ctypes binding of libqmm.so (the C ABI declared in include/qmm.h and
+include/qmm_tp.h).
 
 The library is the product: there is no Python or CPU fallback. Loading fails
 loudly when the shared object is missing.
@@ -38,7 +39,7 @@ GELU = 0
 SILU = 1
 RELU = 2
 
-# Every symbol include/qmm.h declares, with (restype, argtypes).
+# Every symbol include/qmm.h and include/qmm_tp.h declare, with (restype, argtypes).
 _P = ctypes.c_void_p
 _SZ = ctypes.c_size_t
 _I = ctypes.c_int
@@ -95,7 +96,22 @@ SIGNATURES = {
     "qmm_attention_decode_fused_dev": (_I, [_P, _SZ, _I, _I, _I, _P, _P, _F, _F, _P, _P, _P, _I, _P, _P, _F, _P, _P,
                                             _P]),
     "qmm_add_int_dev": (_I, [_P, _I, _P]),
+    # include/qmm_tp.h
+    "qmm_weight_create_row_shard": (_I, [_I, _SZ, _SZ, _P, _SZ, _I, _I, _I, _P]),
+    "qmm_tp_available": (_I, []),
+    "qmm_tp_unique_id": (_I, [_P]),
+    "qmm_tp_init": (_I, [_P, _I, _I, _I, ctypes.c_double, _P]),
+    "qmm_tp_destroy": (_I, [_P]),
+    "qmm_tp_abort": (_I, [_P]),
+    "qmm_tp_rank": (_I, [_P, _P, _P]),
+    "qmm_tp_status": (_I, [_P]),
+    "qmm_tp_wait": (_I, [_P, _P, ctypes.c_double]),
+    "qmm_tp_column_forward": (_I, [_P, _P, _P, _SZ, _P, _I, _P]),
+    "qmm_tp_row_forward": (_I, [_P, _P, _P, _SZ, _P, _I, _P]),
+    "qmm_tp_all_gather_f32": (_I, [_P, _P, _P, _SZ, _P]),
+    "qmm_tp_all_reduce_f32": (_I, [_P, _P, _SZ, _P]),
 }
+TP_UNIQUE_ID_BYTES = 128
 
 
 class QmmError(RuntimeError):

@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "../../include/qmm.h"
+#include "../../include/qmm_tp.h"
 #include "qmm_common.cuh"
 #include "qmm_kernels.cuh"
 
@@ -62,6 +63,13 @@ int fail(int status, const std::string& msg) {
     t_last_error = msg;
     return status;
 }
+}  // namespace
+
+namespace qmm {
+int set_last_error(int status, const std::string& msg) { return fail(status, msg); }
+}  // namespace qmm
+
+namespace {
 int cuda_fail(cudaError_t e, const char* where) {
     cudaGetLastError();  // clear sticky-free errors so later calls are not poisoned
     return fail(QMM_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
@@ -506,6 +514,28 @@ QMM_API int qmm_weight_create(int dtype, size_t n, size_t k, const uint8_t* host
 QMM_API int qmm_weight_create_from_device(int dtype, size_t n, size_t k, const uint8_t* dev_bytes, size_t len,
                                           int device, qmm_weight** out) {
     return weight_create_impl(dtype, n, k, dev_bytes, len, device, true, out);
+}
+
+QMM_API int qmm_weight_create_row_shard(int dtype, size_t n, size_t k, const uint8_t* host_bytes, size_t len,
+                                        int rank, int world, int device, qmm_weight** out) {
+    if (!out || !host_bytes) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    *out = nullptr;
+    int rc = check_shape(dtype, 0, k, n, len);
+    if (rc) return rc;
+    if (world < 1 || rank < 0 || rank >= world) return fail(QMM_ERR_INVALID_INPUT, "bad rank / world");
+    const size_t nb = k / QK;
+    if (nb % (size_t)world) return fail(QMM_ERR_SHAPE_MISMATCH, "k/32 blocks do not split evenly over the ranks");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(QMM_ERR_NO_DEVICE, "no CUDA device");
+    }
+    if (device < 0 || device >= ndev) return fail(QMM_ERR_INVALID_INPUT, "bad device index");
+    const size_t bb = (size_t)block_bytes(dtype), row = nb * bb, local = row / (size_t)world;
+    const uint8_t* src = host_bytes + (size_t)rank * local;
+    return weight_build(dtype, n, k / (size_t)world, device, 0,
+                        [&](uint8_t* d) { return cudaMemcpy2D(d, local, src, row, local, n, cudaMemcpyHostToDevice); },
+                        out);
 }
 
 QMM_API int qmm_weight_fuse_rows(const qmm_weight* const* parts, size_t count, qmm_weight** out) {

@@ -1,0 +1,434 @@
+// Tensor-parallel C ABI of libqmm.so (declared in include/qmm_tp.h): NCCL
+// communicators with host-side time limits, and the column-/row-parallel
+// quantised linears on top of the single-GPU entry points of include/qmm.h.
+//
+// NCCL is resolved with dlopen at the first use, so the library links no NCCL
+// and a process that already loaded one (PyTorch's libnccl.so.2) shares it.
+// Every communicator is created non-blocking (ncclConfig_t.blocking = 0):
+// nothing here ever blocks inside NCCL. Waits are host polls of
+// ncclCommGetAsyncError (and cudaStreamQuery) with a time limit; an NCCL error
+// or a limit that runs out aborts the communicator (ncclCommAbort, which also
+// ends its kernels still in flight) and returns QMM_ERR_NCCL / QMM_ERR_TIMEOUT,
+// the reference FFI's "errors become codes" convention
+// (llminference/main/features/inference/ffi/main/src/lib.rs:12-21).
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+
+#include "../../include/qmm.h"
+#include "../../include/qmm_tp.h"
+#include "qmm_common.cuh"
+
+namespace qmm {
+int set_last_error(int status, const std::string& msg);
+void note_launch();
+}  // namespace qmm
+
+static_assert(sizeof(ncclUniqueId) == QMM_TP_UNIQUE_ID_BYTES, "unique id size");
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+int fail(int status, const std::string& msg) { return qmm::set_last_error(status, msg); }
+
+// ---- NCCL entry points, resolved at run time ---------------------------------------
+struct NcclApi {
+    bool ok = false;
+    std::string why;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+template <class F>
+bool bind(void* h, const char* name, F& fn) {
+    fn = reinterpret_cast<F>(dlsym(h, name));
+    return fn != nullptr;
+}
+
+NcclApi load_nccl() {
+    NcclApi a;
+    const char* env = std::getenv("QMM_NCCL_LIBRARY");
+    void* h = nullptr;
+    if (env && *env) {
+        h = dlopen(env, RTLD_NOW | RTLD_LOCAL);
+    } else {
+        h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+    }
+    if (!h) {
+        const char* e = dlerror();
+        a.why = std::string("cannot load NCCL: ") + (e ? e : "unknown");
+        return a;
+    }
+    bool ok = bind(h, "ncclGetUniqueId", a.GetUniqueId) && bind(h, "ncclCommInitRankConfig", a.CommInitRankConfig) &&
+              bind(h, "ncclCommGetAsyncError", a.CommGetAsyncError) && bind(h, "ncclCommAbort", a.CommAbort) &&
+              bind(h, "ncclCommFinalize", a.CommFinalize) && bind(h, "ncclCommDestroy", a.CommDestroy) &&
+              bind(h, "ncclAllGather", a.AllGather) && bind(h, "ncclAllReduce", a.AllReduce) &&
+              bind(h, "ncclGetErrorString", a.GetErrorString);
+    if (!ok) {
+        a.why = "the NCCL library lacks a needed entry point";
+        return a;
+    }
+    a.ok = true;
+    return a;
+}
+
+const NcclApi& nccl() {
+    static const NcclApi api = load_nccl();
+    return api;
+}
+
+std::string nccl_str(ncclResult_t r) {
+    const char* s = nccl().GetErrorString ? nccl().GetErrorString(r) : nullptr;
+    return s ? s : ("NCCL error " + std::to_string((int)r));
+}
+
+double seconds_since(Clock::time_point t0) {
+    return std::chrono::duration<double>(Clock::now() - t0).count();
+}
+
+struct DevGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DevGuard(int dev) {
+        if (dev < 0) return;
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (dev != prev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DevGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Rank-major [world][m][nl] -> [m][world * nl].
+__global__ void tp_reorder_kernel(const float* __restrict__ g, float* __restrict__ y, int m, int nl, int world) {
+    const int64_t total = (int64_t)m * nl * world;
+    const int64_t row = (int64_t)nl * world;
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = o / row, c = o - i * row;
+        const int64_t r = c / nl, j = c - r * nl;
+        y[o] = g[(r * m + i) * nl + j];
+    }
+}
+
+}  // namespace
+
+struct qmm_tp_comm {
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1, device = 0;
+    double timeout_s = 60.0;
+    std::atomic<int> aborted{0};
+    std::mutex mu;  // guards the gather buffer
+    float* gbuf = nullptr;
+    size_t gbytes = 0;
+};
+
+namespace {
+
+void abort_comm(qmm_tp_comm* c) {
+    int expected = 0;
+    if (c->comm && c->aborted.compare_exchange_strong(expected, 1)) nccl().CommAbort(c->comm);
+}
+
+// Polls the communicator until it leaves ncclInProgress (non-blocking init,
+// finalize, or an enqueue that returned ncclInProgress). Aborts on error or
+// when `limit_s` runs out.
+int settle(qmm_tp_comm* c, double limit_s, const char* what) {
+    const auto t0 = Clock::now();
+    for (;;) {
+        ncclResult_t st = ncclInProgress;
+        const ncclResult_t r = nccl().CommGetAsyncError(c->comm, &st);
+        if (r != ncclSuccess) {
+            abort_comm(c);
+            return fail(QMM_ERR_NCCL, std::string(what) + ": ncclCommGetAsyncError: " + nccl_str(r));
+        }
+        if (st == ncclSuccess) return QMM_OK;
+        if (st != ncclInProgress) {
+            abort_comm(c);
+            return fail(QMM_ERR_NCCL, std::string(what) + ": " + nccl_str(st));
+        }
+        if (seconds_since(t0) > limit_s) {
+            abort_comm(c);
+            return fail(QMM_ERR_TIMEOUT, std::string(what) + " did not complete within " + std::to_string(limit_s) +
+                                             " s; communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+// Result of an enqueue on a non-blocking communicator.
+int enqueued(qmm_tp_comm* c, ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return QMM_OK;
+    if (r == ncclInProgress) return settle(c, c->timeout_s, what);
+    abort_comm(c);
+    return fail(QMM_ERR_NCCL, std::string(what) + ": " + nccl_str(r));
+}
+
+int usable(const qmm_tp_comm* c) {
+    if (!c) return fail(QMM_ERR_INVALID_INPUT, "null communicator");
+    if (c->aborted.load()) return fail(QMM_ERR_NCCL, "communicator was aborted");
+    return QMM_OK;
+}
+
+int gather_buffer(qmm_tp_comm* c, size_t bytes, cudaStream_t st, float** out) {
+    std::lock_guard<std::mutex> lock(c->mu);
+    if (c->gbytes < bytes) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+            return fail(QMM_ERR_INVALID_INPUT, "gather buffer must grow during stream capture; run once uncaptured");
+        if (c->gbuf) {
+            cudaStreamSynchronize(st);
+            cudaFree(c->gbuf);
+            c->gbuf = nullptr;
+            c->gbytes = 0;
+        }
+        const cudaError_t e = cudaMalloc(&c->gbuf, bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(QMM_ERR_CUDA, std::string("gather buffer: ") + cudaGetErrorString(e));
+        }
+        c->gbytes = bytes;
+    }
+    *out = c->gbuf;
+    return QMM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+QMM_API int qmm_tp_available(void) { return nccl().ok ? 1 : 0; }
+
+QMM_API int qmm_tp_unique_id(uint8_t out[QMM_TP_UNIQUE_ID_BYTES]) {
+    if (!out) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (!nccl().ok) return fail(QMM_ERR_NCCL, nccl().why);
+    ncclUniqueId id;
+    const ncclResult_t r = nccl().GetUniqueId(&id);
+    if (r != ncclSuccess) return fail(QMM_ERR_NCCL, "ncclGetUniqueId: " + nccl_str(r));
+    std::memcpy(out, id.internal, QMM_TP_UNIQUE_ID_BYTES);
+    return QMM_OK;
+}
+
+QMM_API int qmm_tp_init(const uint8_t id[QMM_TP_UNIQUE_ID_BYTES], int world, int rank, int device, double timeout_s,
+                        qmm_tp_comm** out) {
+    if (!id || !out) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    *out = nullptr;
+    if (world < 1 || rank < 0 || rank >= world) return fail(QMM_ERR_INVALID_INPUT, "bad rank / world");
+    if (!(timeout_s > 0.0)) return fail(QMM_ERR_INVALID_INPUT, "timeout must be positive");
+    if (!nccl().ok) return fail(QMM_ERR_NCCL, nccl().why);
+    DevGuard guard(device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    int dev = device;
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        dev = -1;  // no CUDA context: only a stand-in NCCL can get further
+    }
+    ncclUniqueId uid;
+    std::memcpy(uid.internal, id, QMM_TP_UNIQUE_ID_BYTES);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    qmm_tp_comm* c = new qmm_tp_comm;
+    c->rank = rank;
+    c->world = world;
+    c->device = dev;
+    c->timeout_s = timeout_s;
+    const ncclResult_t r = nccl().CommInitRankConfig(&c->comm, world, uid, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        if (c->comm) nccl().CommAbort(c->comm);
+        delete c;
+        return fail(QMM_ERR_NCCL, "ncclCommInitRankConfig: " + nccl_str(r));
+    }
+    const int rc = settle(c, timeout_s, "communicator init");
+    if (rc) {
+        delete c;  // settle() aborted it
+        return rc;
+    }
+    *out = c;
+    return QMM_OK;
+}
+
+QMM_API int qmm_tp_abort(qmm_tp_comm* c) {
+    if (!c) return fail(QMM_ERR_INVALID_INPUT, "null communicator");
+    abort_comm(c);
+    return QMM_OK;
+}
+
+QMM_API int qmm_tp_destroy(qmm_tp_comm* c) {
+    if (!c) return QMM_OK;
+    int rc = QMM_OK;
+    {
+        DevGuard guard(c->device);
+        if (!c->aborted.load() && c->comm) {
+            // finalize flushes outstanding work; bounded like every other wait
+            ncclResult_t r = nccl().CommFinalize(c->comm);
+            if (r == ncclSuccess || r == ncclInProgress) rc = settle(c, c->timeout_s, "communicator finalize");
+            else {
+                abort_comm(c);
+                rc = fail(QMM_ERR_NCCL, "ncclCommFinalize: " + nccl_str(r));
+            }
+            if (!c->aborted.load()) nccl().CommDestroy(c->comm);
+        }
+        if (c->gbuf) cudaFree(c->gbuf);
+    }
+    delete c;
+    return rc;
+}
+
+QMM_API int qmm_tp_rank(const qmm_tp_comm* c, int* rank, int* world) {
+    if (!c) return fail(QMM_ERR_INVALID_INPUT, "null communicator");
+    if (rank) *rank = c->rank;
+    if (world) *world = c->world;
+    return QMM_OK;
+}
+
+QMM_API int qmm_tp_status(qmm_tp_comm* c) {
+    int rc = usable(c);
+    if (rc) return rc;
+    ncclResult_t st = ncclSuccess;
+    const ncclResult_t r = nccl().CommGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess || (st != ncclSuccess && st != ncclInProgress)) {
+        abort_comm(c);
+        return fail(QMM_ERR_NCCL, "communicator error: " + nccl_str(r != ncclSuccess ? r : st));
+    }
+    return QMM_OK;
+}
+
+QMM_API int qmm_tp_wait(qmm_tp_comm* c, void* stream, double timeout_s) {
+    int rc = usable(c);
+    if (rc) return rc;
+    if (!(timeout_s > 0.0)) return fail(QMM_ERR_INVALID_INPUT, "timeout must be positive");
+    DevGuard guard(c->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    const cudaStream_t st = (cudaStream_t)stream;
+    const auto t0 = Clock::now();
+    auto drain = [&]() {
+        // after an abort NCCL's kernels exit; let the stream run dry (bounded)
+        const auto t1 = Clock::now();
+        while (cudaStreamQuery(st) == cudaErrorNotReady && seconds_since(t1) < 10.0)
+            std::this_thread::sleep_for(std::chrono::microseconds(200));
+        cudaGetLastError();
+    };
+    for (;;) {
+        ncclResult_t as = ncclSuccess;
+        const ncclResult_t r = nccl().CommGetAsyncError(c->comm, &as);
+        if (r != ncclSuccess || (as != ncclSuccess && as != ncclInProgress)) {
+            abort_comm(c);
+            drain();
+            return fail(QMM_ERR_NCCL, "communicator error: " + nccl_str(r != ncclSuccess ? r : as));
+        }
+        const cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) return QMM_OK;
+        if (q != cudaErrorNotReady) {
+            cudaGetLastError();
+            return fail(QMM_ERR_CUDA, std::string("cudaStreamQuery: ") + cudaGetErrorString(q));
+        }
+        if (seconds_since(t0) > timeout_s) {
+            abort_comm(c);
+            drain();
+            return fail(QMM_ERR_TIMEOUT, "stream work did not finish within " + std::to_string(timeout_s) +
+                                             " s; communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+QMM_API int qmm_tp_all_gather_f32(qmm_tp_comm* c, const float* send, float* recv, size_t count, void* stream) {
+    int rc = usable(c);
+    if (rc) return rc;
+    if (!send || !recv) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (count == 0) return QMM_OK;
+    DevGuard guard(c->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    return enqueued(c, nccl().AllGather(send, recv, count, ncclFloat32, c->comm, (cudaStream_t)stream),
+                    "ncclAllGather");
+}
+
+QMM_API int qmm_tp_all_reduce_f32(qmm_tp_comm* c, float* buf, size_t count, void* stream) {
+    int rc = usable(c);
+    if (rc) return rc;
+    if (!buf) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    if (count == 0) return QMM_OK;
+    DevGuard guard(c->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    return enqueued(c, nccl().AllReduce(buf, buf, count, ncclFloat32, ncclSum, c->comm, (cudaStream_t)stream),
+                    "ncclAllReduce");
+}
+
+QMM_API int qmm_tp_column_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t m, float* y,
+                                  int act, void* stream) {
+    int rc = usable(c);
+    if (rc) return rc;
+    if (!shard || !x || !y) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    size_t nl = 0;
+    int wdev = -1;
+    rc = qmm_weight_info(shard, nullptr, &nl, nullptr, nullptr, &wdev);
+    if (rc) return rc;
+    if (wdev != c->device) return fail(QMM_ERR_INVALID_INPUT, "shard lives on another device than the communicator");
+    if (m == 0) return QMM_OK;
+    DevGuard guard(c->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (c->world == 1) return qmm_linear_forward(shard, x, m, y, act, stream);
+    if (m == 1) {
+        // [1][world * nl] is already rank-major: gather in place
+        float* slot = y + (size_t)c->rank * nl;
+        rc = qmm_linear_forward(shard, x, m, slot, act, stream);
+        if (rc) return rc;
+        return enqueued(c, nccl().AllGather(slot, y, nl, ncclFloat32, c->comm, st), "ncclAllGather");
+    }
+    if (m * nl * (size_t)c->world > (size_t)INT32_MAX) return fail(QMM_ERR_INVALID_INPUT, "output too large");
+    float* g = nullptr;
+    rc = gather_buffer(c, m * nl * (size_t)c->world * sizeof(float), st, &g);
+    if (rc) return rc;
+    float* local = g + (size_t)c->rank * m * nl;
+    rc = qmm_linear_forward(shard, x, m, local, act, stream);
+    if (rc) return rc;
+    rc = enqueued(c, nccl().AllGather(local, g, m * nl, ncclFloat32, c->comm, st), "ncclAllGather");
+    if (rc) return rc;
+    const int64_t total = (int64_t)m * nl * c->world;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+    qmm::note_launch();
+    tp_reorder_kernel<<<blocks, 256, 0, st>>>(g, y, (int)m, (int)nl, c->world);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(QMM_ERR_CUDA, std::string("tp_reorder_kernel: ") + cudaGetErrorString(e));
+    return QMM_OK;
+}
+
+QMM_API int qmm_tp_row_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x_local, size_t m, float* y,
+                               int act, void* stream) {
+    int rc = usable(c);
+    if (rc) return rc;
+    if (!shard || !x_local || !y) return fail(QMM_ERR_INVALID_INPUT, "null pointer");
+    size_t n = 0;
+    int wdev = -1;
+    rc = qmm_weight_info(shard, nullptr, &n, nullptr, nullptr, &wdev);
+    if (rc) return rc;
+    if (wdev != c->device) return fail(QMM_ERR_INVALID_INPUT, "shard lives on another device than the communicator");
+    if (m == 0) return QMM_OK;
+    DevGuard guard(c->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    rc = qmm_linear_forward(shard, x_local, m, y, act, stream);
+    if (rc || c->world == 1) return rc;
+    return enqueued(c, nccl().AllReduce(y, y, m * n, ncclFloat32, ncclSum, c->comm, (cudaStream_t)stream),
+                    "ncclAllReduce");
+}
+
+}  // extern "C"

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _declared_symbols():
-    hdr = open(os.path.join(ROOT, "include", "qmm.h")).read()
+    hdr = "".join(open(os.path.join(ROOT, "include", h)).read() for h in ("qmm.h", "qmm_tp.h"))
     return sorted(set(re.findall(r"QMM_API\s+[\w\s\*]+?\b(qmm_\w+)\s*\(", hdr)))
 
 
@@ -24,7 +24,7 @@ def test_header_symbols_exported(qlib):
     syms = _declared_symbols()
     assert len(syms) >= 25
     for s in syms:
-        assert hasattr(qlib, s), f"{s} declared in include/qmm.h but not exported"
+        assert hasattr(qlib, s), f"{s} declared in include/ but not exported"
         assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
     assert set(_lib.SIGNATURES) == set(syms)
 

@@ -1,8 +1,8 @@
 """Benchmark of the quantized-matmul hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-sub]
-                    [--workload gemma-q8-sweep|q4-gemv|llama70b|llama70b-gate|prefill|gemma-decode]
-                    [--batch B]
+                    [--workload llama70b-megatron|llama70b|gemma-q8-sweep|q4-gemv|llama70b-gate|prefill|
+                                gemma-decode] [--batch B]
 
 Workloads (synthetic, seeded, weights ~N(0, 0.02)
 quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
@@ -14,13 +14,19 @@ quantised by this library's bit-exact device quantisers, x ~ N(0, 1)):
       from HBM every step.
   q4-gemv: Q4_0 [6912 x 1152] x f32 [1152], batch 1, 64 weight
       copies rotated (287 MB > L2).
-  llama70b (default, configs[4]): Q4_0 gate/up 8192->28672, down
+  llama70b-megatron (default, configs[4]): Q4_0 gate/up 8192->28672, down
       28672->8192, Q8_0 lm_head 8192->128256, batch 1 and 32 (1.5 GB of
       weights per batch) -- the configuration BASELINE defines at 1/2/4/8
-      GPUs. The default run (no --workload) prints its line with one
-      sub-record per other configuration under "workloads" (one GPU only):
-      gemma-q8-sweep, q4-gemv, prefill, gemma-decode at batch 1, 16 and 64,
-      each timed in the same run with its own roofline, e2e and CPU baseline.
+      GPUs -- with gate and up fused (SwiGLU epilogue) feeding down directly:
+      with N GPUs one all-reduce per FFN and one all-gather for lm_head.
+      Bytes are counted as the reference's four GEMVs. The default run (no
+      --workload) prints its line with one sub-record per other configuration
+      under "workloads" (one GPU): llama70b, gemma-q8-sweep, q4-gemv, prefill,
+      gemma-decode at batch 1, 16 and 64, each timed in the same run with its
+      own roofline, e2e and CPU baseline; with N GPUs the llama70b record.
+  llama70b (configs[4] as written): the same four projections as separate
+      GEMVs; with N GPUs gate/up/lm_head column-parallel with an all-gather
+      each, down row-parallel with an all-reduce.
   llama70b-gate (one projection of configs[4]): Q4_0 8192->28672, batch 1,
       two weight copies (264 MB > L2); the small case for streaming-kernel
       profiles.
@@ -41,9 +47,11 @@ captured.
 
 Metric: the reference's own bandwidth formula (quantize.rs:399-404),
     GB/s = sum over GEMVs of (M*K*4 + N*(K/32)*block_bytes + M*N*4) / time.
-With N GPUs the projections are tensor-parallel (column-parallel q/k/v/gate/
-up/lm_head joined by an NCCL all-gather, row-parallel o/down joined by an
-all-reduce), total work fixed ("strong" scaling); value is the whole-job rate.
+With N GPUs the projections are tensor-parallel through the library's own
+NCCL communicator (include/qmm_tp.h: column-parallel q/k/v/gate/up/lm_head
+joined by an all-gather, row-parallel o/down by an all-reduce; the process
+group is gloo, for barriers and the timing max only), total work fixed
+("strong" scaling); value is the whole-job rate.
 
 `--impl reference` times the reference's CPU path (the C++ restatement in
 oracle/, AVX2+FMA with OpenMP over all host cores; the Rust original cannot be
@@ -228,14 +236,18 @@ class ClockSampler:
 MIN_TIMED_S = 0.1  # every timed region is repeated until the repetitions cover this
 
 
-def timed_regions(enqueue, stream, dev, steps, world, sampler):
+def timed_regions(enqueue, stream, dev, steps, world, sampler, sync=None):
     """Times `steps` steps with CUDA events on `stream` (enqueue(steps) issues
     them), barrier + synchronize on both sides, max over ranks; the K-step
     region is repeated until the repetitions cover MIN_TIMED_S (at least
     once), and the median repetition is reported. Returns (ms of the median
-    region, every region's ms, clock samples taken during the regions)."""
+    region, every region's ms, clock samples taken during the regions).
+    `sync` replaces the device synchronize (the tensor-parallel runs wait
+    through the communicator, with a time limit)."""
     import torch
     import torch.distributed as dist
+
+    sync = sync or (lambda: torch.cuda.synchronize(dev))
 
     def barrier():
         if world > 1:
@@ -244,16 +256,16 @@ def timed_regions(enqueue, stream, dev, steps, world, sampler):
     def one():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
-        torch.cuda.synchronize(dev)
+        sync()
         with torch.cuda.stream(stream):
             e0.record(stream)
             enqueue(steps)
             e1.record(stream)
-        torch.cuda.synchronize(dev)
+        sync()
         barrier()
         ms = e0.elapsed_time(e1)
-        if world > 1:  # the same number of collectives on every rank
-            t = torch.tensor([ms], device=dev)
+        if world > 1:  # the same number of collectives on every rank (host tensors: gloo)
+            t = torch.tensor([ms])
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
         return ms
@@ -364,16 +376,39 @@ def run_ours(args, rank, world, local_rank):
                      for (_, kl, nl, dt, kind, k, n) in problems)
     metric, unit, div = metric_info(wl)
 
-    # ---- CUDA graphs ---------------------------------------------------------------------
+    def sync():
+        """Device synchronize; with a communicator, its bounded wait (a stuck
+        collective aborts the communicator and raises instead of hanging)."""
+        if comm is not None:
+            _lib.check(comm.wait(120.0, stream))
+        else:
+            torch.cuda.synchronize(dev)
+
+    # ---- CUDA graphs (one GPU) ---------------------------------------------------------------
     # A timed region of K steps runs step i on weight copy i % copies: whole
     # passes over the copies as one graph each, then one graph of the
     # remaining K % copies steps (copies 0, 1, ...), so a region is at most
-    # K // copies + 1 graph launches whatever K is.
+    # K // copies + 1 graph launches whatever K is. With N GPUs the steps are
+    # enqueued directly: the library's NCCL communicator is non-blocking (its
+    # launches may complete on NCCL's own thread), which stream capture does
+    # not take.
     graphs = {}
     with torch.cuda.stream(stream):
         for c in range(copies):
             one_step(c)  # warm the planner/tensor-map caches outside capture
-        stream.synchronize()
+        sync()
+    if comm is not None:
+        n0 = L.qmm_launch_count()
+        with torch.cuda.stream(stream):
+            one_step(0)
+        sync()
+        launches_per_step = L.qmm_launch_count() - n0
+
+        def run_steps(n):
+            for i in range(n):
+                one_step(i % copies)
+    else:
+        run_steps = None
 
         def capture(n):
             g = torch.cuda.CUDAGraph()
@@ -388,23 +423,24 @@ def run_ours(args, rank, world, local_rank):
         for n in {copies, args.steps % copies, args.warmup % copies}:
             if n > 1 and n not in graphs:
                 graphs[n] = capture(n)[0]
-    torch.cuda.synchronize(dev)
+    sync()
 
-    def run_steps(n):
-        """Exactly n steps, step i on weight copy i % copies."""
-        for _ in range(n // copies):
-            graphs[copies].replay()
-        r = n % copies
-        if r in graphs:
-            graphs[r].replay()
-        else:
-            for _ in range(r):  # (only for counts no graph was captured for)
-                graphs[1].replay()
+    if run_steps is None:
+        def run_steps(n):
+            """Exactly n steps, step i on weight copy i % copies."""
+            for _ in range(n // copies):
+                graphs[copies].replay()
+            r = n % copies
+            if r in graphs:
+                graphs[r].replay()
+            else:
+                for _ in range(r):  # (only for counts no graph was captured for)
+                    graphs[1].replay()
 
     # warm-up
     with torch.cuda.stream(stream):
         run_steps(args.warmup)
-    stream.synchronize()
+    sync()
 
     # timed regions: K steps each, events on the launching stream, max over
     # ranks, repeated to >= 100 ms, median reported
@@ -412,8 +448,8 @@ def run_ours(args, rank, world, local_rank):
     with sampler:
         with torch.cuda.stream(stream):
             run_steps(max(args.warmup, 3))  # clock soak right before the timed region
-        torch.cuda.synchronize(dev)
-        ms, regions, n_timed = timed_regions(run_steps, stream, dev, args.steps, world, sampler)
+        sync()
+        ms, regions, n_timed = timed_regions(run_steps, stream, dev, args.steps, world, sampler, sync)
     ms_per_step = ms / args.steps
     value = steps_work * args.steps / (ms / 1e3) / div
 
@@ -432,7 +468,7 @@ def run_ours(args, rank, world, local_rank):
     # graphs that hold NCCL calls are released before the communicator goes
     graphs.clear()
     if comm is not None:
-        stream.synchronize()
+        sync()
         _lib.check(comm.close())
     line = None
     if rank == 0:
@@ -464,8 +500,9 @@ def run_ours(args, rank, world, local_rank):
                 "algorithmic_bytes_per_step": steps_bytes,
                 "algorithmic_flops_per_step": sum(2 * gemvs_of(kind) * b * k * n for b in wl["batches"]
                                                   for (_, kl, nl, dt, kind, k, n) in problems),
-                "graph": "one CUDA graph per pass over the weight copies plus one for the remaining K % copies steps; "
-                         "PDL between kernels",
+                "graph": ("one CUDA graph per pass over the weight copies plus one for the remaining K % copies "
+                          "steps; PDL between kernels" if comm is None else
+                          "direct launches (non-blocking NCCL communicator; no stream capture); PDL between kernels"),
             },
             "roofline": {
                 "bound": "tensor" if wl.get("metric") == "flops" else "hbm",
@@ -576,7 +613,7 @@ def e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, c
                     if (b, pi) in hy:
                         hy[(b, pi)].copy_(dy[(b, pi)], non_blocking=True)
             if comm is not None:
-                _lib.check(comm.wait(120.0))
+                _lib.check(comm.wait(120.0, stream))
             else:
                 stream.synchronize()
 
@@ -591,7 +628,7 @@ def e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, c
         dist.barrier()
     dt_s = time.perf_counter() - t0
     if world > 1:
-        t = torch.tensor([dt_s], device=dev)
+        t = torch.tensor([dt_s])
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt_s = float(t.item())
     work_step = sum(gemvs_of(kind) * work(wl, b, k, n, d) for b in wl["batches"]
@@ -899,9 +936,12 @@ def run_decode_reference(args, rank, world):
         "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
-DEFAULT_WORKLOAD = "llama70b"  # the configuration defined at 1/2/4/8 GPUs
+# BASELINE configs[4], the configuration defined at 1/2/4/8 GPUs, in its
+# Megatron-paired form (one all-reduce per FFN, no all-gather between gate/up
+# and down); the literal form (all-gather after gate/up) is a sub-record
+DEFAULT_WORKLOAD = "llama70b-megatron"
 # the other BASELINE configurations, timed in the same default run (one GPU)
-SUB_WORKLOADS = [("llama70b-megatron", None), ("gemma-q8-sweep", None), ("q4-gemv", None), ("prefill", None),
+SUB_WORKLOADS = [("llama70b", None), ("gemma-q8-sweep", None), ("q4-gemv", None), ("prefill", None),
                  ("gemma-decode", 1),
                  ("gemma-decode", 16), ("gemma-decode", 64)]
 
@@ -913,8 +953,10 @@ def _init_dist(world, local_rank):
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+        # the process group is the control plane only (barriers, the timing
+        # max, the communicator's unique id): gloo on the host. Every byte of
+        # the data path moves through the library's own NCCL communicator.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
 
 
 def _run_one(args, rank, world, local_rank, shared_decode=None):
@@ -960,10 +1002,10 @@ def main(argv=None):
         line = _run_one(args, rank, world, local_rank)
         if default_run and not args.no_sub:
             # every other BASELINE configuration, timed in this same run (one
-            # GPU); with N GPUs the Megatron-paired form of the same layer set
+            # GPU); with N GPUs the literal (all-gather) form of the same layer set
             subs = {}
             shared = None
-            for name, batch in (SUB_WORKLOADS if world == 1 else [("llama70b-megatron", None)]):
+            for name, batch in (SUB_WORKLOADS if world == 1 else [("llama70b", None)]):
                 sub = argparse.Namespace(**vars(args))
                 sub.workload, sub.copies = name, None
                 if batch is not None:

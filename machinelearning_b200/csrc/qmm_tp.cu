@@ -104,6 +104,14 @@ double seconds_since(Clock::time_point t0) {
     return std::chrono::duration<double>(Clock::now() - t0).count();
 }
 
+// Pause between polls: yield for the first 2 ms of a wait (a collective's
+// enqueue on a non-blocking communicator settles in tens of microseconds, and a
+// sleeping poll would add the timer's granularity to every call), then sleep.
+void poll_pause(Clock::time_point t0) {
+    if (seconds_since(t0) < 2e-3) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(100));
+}
+
 struct DevGuard {
     int prev = -1;
     bool ok = true;
@@ -170,7 +178,7 @@ int settle(qmm_tp_comm* c, double limit_s, const char* what) {
             return fail(QMM_ERR_TIMEOUT, std::string(what) + " did not complete within " + std::to_string(limit_s) +
                                              " s; communicator aborted");
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        poll_pause(t0);
     }
 }
 
@@ -346,7 +354,7 @@ QMM_API int qmm_tp_wait(qmm_tp_comm* c, void* stream, double timeout_s) {
             return fail(QMM_ERR_TIMEOUT, "stream work did not finish within " + std::to_string(timeout_s) +
                                              " s; communicator aborted");
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
+        poll_pause(t0);
     }
 }
 

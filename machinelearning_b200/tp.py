@@ -131,10 +131,12 @@ class TpComm:
         """One poll of the communicator's error state (a status code, never raises)."""
         return _lib.lib().qmm_tp_status(self._h)
 
-    def wait(self, timeout_s: float | None = None) -> int:
-        """Waits for the current stream's work with the communicator watched;
-        a status code (QMM_ERR_TIMEOUT / QMM_ERR_NCCL abort the communicator)."""
-        return _lib.lib().qmm_tp_wait(self._h, ctypes.c_void_p(_stream_ptr(self.device)),
+    def wait(self, timeout_s: float | None = None, stream: torch.cuda.Stream | None = None) -> int:
+        """Waits for `stream`'s work (default: the current stream) with the
+        communicator watched; a status code (QMM_ERR_TIMEOUT / QMM_ERR_NCCL
+        abort the communicator)."""
+        sp = stream.cuda_stream if stream is not None else _stream_ptr(self.device)
+        return _lib.lib().qmm_tp_wait(self._h, ctypes.c_void_p(sp),
                                       float(timeout_s if timeout_s is not None else self.timeout_s))
 
     def all_gather(self, send: torch.Tensor) -> torch.Tensor:

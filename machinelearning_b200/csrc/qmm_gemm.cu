@@ -54,7 +54,6 @@ constexpr int BM = 128;            // tokens per accumulator (MMA M, TMEM lanes)
 constexpr int BN = 128;            // weight rows per tile by default (MMA N, TMEM columns); 160 also built
 constexpr int BK = 64;             // f16 elements per K step: one 128-byte swizzle row
 constexpr int kStepsPerChunk = 4;  // a raw chunk is 8 blocks = 256 elements
-constexpr int SR = 2;              // raw chunk stages
 // Per weight-tile width W (128 or 160 rows): W / 16 dequantising (then
 // epilogue) warps, one (row, block) per thread per K step; 2 + W / 16 + 1 warps
 // in all (x16 producer, MMA issuer, dequantisers, raw-chunk producer).
@@ -85,6 +84,7 @@ struct GArgs {
     const float* xs;     // per-row activation scales
     float* y;
     int M, N, K, ksteps, weights_immutable;
+    int xrows;           // token rows one x16 box carries (T == 1: M rounded up to 8; else BM)
     int* err;
     int ks, cps;         // K slices (blockIdx.z) and raw chunks per slice
     float* partial;      // [ks][M][N] unscaled partial tiles (ks > 1)
@@ -96,9 +96,28 @@ struct GArgs {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-__host__ __device__ constexpr size_t gemm_smem_bytes(int qt, int T, int W) {
-    return 1024 + (size_t)a_stages(qt, T, W) * T * kTileBytes + (size_t)b_stages(qt, T, W) * W * BK * 2 +
-           (size_t)SR * W * raw_pitch(qt) + (2 * a_stages(qt, T, W) + 2 * b_stages(qt, T, W) + 2 * SR + 1) * 8 + 16;
+// Half-height token tiles (H: at most 64 tokens, MMA M = 64): x16 stages of
+// 8 KB, twice as many of them in the same space. The x16 copies take ~1.5 us
+// to land (they queue with the raw chunks' HBM loads) and a stage is refilled
+// only when the MMAs that read it complete; twice the copies in flight took
+// the 32-token lm_head from 366 to 339 us on B200.
+__host__ __device__ constexpr int x_stages(int qt, int T, int W, bool h) { return (h ? 2 : 1) * a_stages(qt, T, W); }
+__host__ __device__ constexpr uint32_t x_tile_bytes(bool h) { return (h ? 64u : (uint32_t)BM) * BK * 2; }
+__host__ __device__ constexpr size_t gemm_smem_with(int qt, int T, int W, int sr, bool h) {
+    return 1024 + (size_t)x_stages(qt, T, W, h) * T * x_tile_bytes(h) + (size_t)b_stages(qt, T, W) * W * BK * 2 +
+           (size_t)sr * W * raw_pitch(qt) + (2 * x_stages(qt, T, W, h) + 2 * b_stages(qt, T, W) + 2 * sr + 1) * 8 +
+           16;
+}
+// Raw chunk stages: as many as fit (2..6). A chunk is 4 K steps and its TMA
+// load takes ~2 us to land under load; the narrower tiles have room to keep
+// more of them in flight.
+__host__ __device__ constexpr int raw_stages(int qt, int T, int W, bool h = false) {
+    int sr = 6;
+    while (sr > 2 && gemm_smem_with(qt, T, W, sr, h) > 232448) --sr;
+    return sr;
+}
+__host__ __device__ constexpr size_t gemm_smem_bytes(int qt, int T, int W, bool h = false) {
+    return gemm_smem_with(qt, T, W, raw_stages(qt, T, W, h), h);
 }
 static_assert(gemm_smem_bytes(kQ4_0, 2, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 2, 160) <= 232448 &&
                   gemm_smem_bytes(kQ4_0, 1, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 1, 160) <= 232448 &&
@@ -259,17 +278,21 @@ __global__ void gemm_xprep_kernel(const float* __restrict__ x, int M, int K, __h
     if (threadIdx.x == 0) xs[m] = __int_as_float((e + 127) << 23);
 }
 
-template <int QT, int T, int W>
+template <int QT, int T, int W, bool H>
 __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_constant__ GArgs a) {
-    constexpr int SA = a_stages(QT, T, W), SB = b_stages(QT, T, W);
+    static_assert(!H || T == 1, "half-height token tiles come one per CTA");
+    constexpr int BMk = H ? 64 : BM;                 // MMA M (token rows of a tile)
+    constexpr uint32_t kATile = x_tile_bytes(H);     // x16 stage bytes per token tile
+    constexpr int SA = x_stages(QT, T, W, H), SB = b_stages(QT, T, W);
     constexpr int kDqWarps = dq_warps(W), kDqThreads = dq_threads(W);
     constexpr uint32_t kBTile = (uint32_t)W * BK * 2;  // dequantised weight tile bytes
     constexpr uint32_t kTmemCols = T * W <= 128 ? 128 : (T * W <= 256 ? 256 : 512);
     constexpr int PITCH = raw_pitch(QT);
+    constexpr int SR = raw_stages(QT, T, W, H);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                        // [SA][T] x16 tiles
-    uint8_t* sB = smem + SA * T * kTileBytes;  // [SB] weight tiles
+    uint8_t* sB = smem + SA * T * kATile;      // [SB] weight tiles
     uint8_t* sR = sB + SB * kBTile;            // [SR] raw chunks
     uint64_t* full_a = reinterpret_cast<uint64_t*>(sR + SR * W * PITCH);
     uint64_t* empty_a = full_a + SA;
@@ -316,6 +339,17 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
+    if (a.xrows < BMk) {
+        // Fewer token rows than the MMA is tall (128, or 64 for half-height
+        // tiles): the boxes carry the real rows only, and the rows past them
+        // stay zero in every stage for the whole launch. Zeroed once here,
+        // before any copy lands.
+        const uint32_t z0 = (uint32_t)a.xrows * 128u;
+        for (int s = 0; s < SA * T; ++s)
+            for (uint32_t o = z0 + 16u * threadIdx.x; o < kATile; o += 16u * blockDim.x)
+                *reinterpret_cast<uint4*>(sA + (size_t)s * kATile + o) = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();  // generic writes -> visible to the tensor core
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -337,10 +371,10 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full_a[s], T * kTileBytes);
+                    mbar_arrive_expect_tx(&full_a[s], (uint32_t)T * (uint32_t)a.xrows * 128u);
 #pragma unroll
                     for (int t = 0; t < T; ++t)
-                        tma_load_2d(sA + (s * T + t) * kTileBytes, &a.tmap_x, (rc * kStepsPerChunk + kk) * BK,
+                        tma_load_2d(sA + (s * T + t) * kATile, &a.tmap_x, (rc * kStepsPerChunk + kk) * BK,
                                     m0 + t * BM, &full_a[s]);
                     ++a_issued;
                 }
@@ -385,10 +419,10 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
                 const uint64_t bd = sw128_desc(smem_u32(sB + sb * kBTile));
 #pragma unroll
                 for (int t = 0; t < T; ++t) {
-                    const uint64_t ad = sw128_desc(smem_u32(sA + (sa * T + t) * kTileBytes));
+                    const uint64_t ad = sw128_desc(smem_u32(sA + (sa * T + t) * kATile));
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)  // 32-byte steps inside the swizzle atom
-                        mma_f16_ss(tmem + t * W, ad + 2 * k, bd + 2 * k, gemm_idesc(W), (i | k) != 0 ? 1u : 0u);
+                        mma_f16_ss(tmem + t * W, ad + 2 * k, bd + 2 * k, gemm_idesc(W, BMk), (i | k) != 0 ? 1u : 0u);
                 }
                 // both stages are free once these MMAs have read them
                 mma_commit(&empty_a[sa]);
@@ -444,16 +478,21 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         float* ys = reinterpret_cast<float*>(sA);
 #pragma unroll
         for (int t = 0; t < T; ++t) {
-            const int r = t * BM + q * 32 + lane;  // token row inside the tile
+            // token row inside the tile; an M = 64 accumulator holds row r in
+            // TMEM lane 32 (r / 16) + r % 16: the first 16 lanes of each quarter
+            const int r = H ? q * 16 + (lane & 15) : t * BM + q * 32 + lane;
+            const bool holds = !H || lane < 16;
 #pragma unroll 1
             for (int cb = jq; cb < W / 32; cb += nq) {
                 uint32_t v[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * W + cb * 32), v);
                 float4* dstp = reinterpret_cast<float4*>(ys + r * YP + cb * 32);
+                if (holds) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    dstp[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                          __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+                    for (int j = 0; j < 8; ++j)
+                        dstp[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                              __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+                }
             }
         }
         tc_fence_before();
@@ -466,7 +505,7 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
             const int et = threadIdx.x - 64;  // 0 .. kDqThreads - 1
             float* mine = a.partial + (int64_t)blockIdx.z * a.M * a.N;
             for (int c4 = lane; c4 < W / 4; c4 += 32)
-                for (int r = warp - 2; r < T * BM; r += kDqWarps) {
+                for (int r = warp - 2; r < T * BMk; r += kDqWarps) {
                     const int m = m0 + r, n = n0 + 4 * c4;
                     if (m >= a.M) break;
                     const float4 v = *reinterpret_cast<const float4*>(ys + r * YP + 4 * c4);
@@ -489,7 +528,7 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
             if (store) {
                 __threadfence();
                 for (int c4 = lane; c4 < W / 4; c4 += 32)
-                    for (int r = warp - 2; r < T * BM; r += kDqWarps) {
+                    for (int r = warp - 2; r < T * BMk; r += kDqWarps) {
                         const int m = m0 + r, n = n0 + 4 * c4;
                         if (m >= a.M) break;
                         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -510,7 +549,7 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
             // index li = lane (+32) produces four consecutive outputs
             const bool gvec = ((reinterpret_cast<uintptr_t>(a.gout) & 15) == 0) && (a.ghidden % 4 == 0);
             for (int li = lane; li < W / 8; li += 32)
-            for (int r = warp - 2; r < T * BM && store; r += kDqWarps) {
+            for (int r = warp - 2; r < T * BMk && store; r += kDqWarps) {
                 const int c = 32 * (li >> 2) + 4 * (li & 3);
                 const int64_t i0 = (int64_t)(n0 / 2) + 16 * (li >> 2) + 4 * (li & 3);
                 const int m = m0 + r;
@@ -535,7 +574,7 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         }
         const bool vec = ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) && (a.N % 4 == 0);
         for (int c4 = lane; c4 < W / 4; c4 += 32)
-        for (int r = warp - 2; r < T * BM && store && a.gact < 0; r += kDqWarps) {
+        for (int r = warp - 2; r < T * BMk && store && a.gact < 0; r += kDqWarps) {
             const int n = n0 + 4 * c4;
             const int m = m0 + r;
             if (m >= a.M) break;  // rows are in increasing order
@@ -559,19 +598,29 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
     }
 }
 
-template <int QT>
-const void* pick_t(int T, int W) {
-    if (W == 64) return T == 1 ? (const void*)gemm_kernel<QT, 1, 64> : (const void*)gemm_kernel<QT, 2, 64>;
-    if (W == 224) return (const void*)gemm_kernel<QT, 1, 224>;
-    if constexpr (QT != kQ8_0) {
-        if (W == 160) return T == 1 ? (const void*)gemm_kernel<QT, 1, 160> : (const void*)gemm_kernel<QT, 2, 160>;
+template <int QT, bool H>
+const void* pick_w(int T, int W) {
+    if constexpr (H) {
+        if (W == 64) return (const void*)gemm_kernel<QT, 1, 64, true>;
+        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224, true>;
+        if constexpr (QT != kQ8_0) {
+            if (W == 160) return (const void*)gemm_kernel<QT, 1, 160, true>;
+        }
+        return (const void*)gemm_kernel<QT, 1, BN, true>;
+    } else {
+        if (W == 64) return T == 1 ? (const void*)gemm_kernel<QT, 1, 64, false> : (const void*)gemm_kernel<QT, 2, 64, false>;
+        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224, false>;
+        if constexpr (QT != kQ8_0) {
+            if (W == 160)
+                return T == 1 ? (const void*)gemm_kernel<QT, 1, 160, false> : (const void*)gemm_kernel<QT, 2, 160, false>;
+        }
+        return T == 1 ? (const void*)gemm_kernel<QT, 1, BN, false> : (const void*)gemm_kernel<QT, 2, BN, false>;
     }
-    return T == 1 ? (const void*)gemm_kernel<QT, 1, BN> : (const void*)gemm_kernel<QT, 2, BN>;
 }
-const void* gemm_kernel_for(int qt, int T, int W) {
-    if (qt == kQ8_0) return pick_t<kQ8_0>(T, W);
-    if (qt == kQ4_0) return pick_t<kQ4_0>(T, W);
-    return pick_t<kQ4_1>(T, W);
+const void* gemm_kernel_for(int qt, int T, int W, bool h) {
+    if (qt == kQ8_0) return h ? pick_w<kQ8_0, true>(T, W) : pick_w<kQ8_0, false>(T, W);
+    if (qt == kQ4_0) return h ? pick_w<kQ4_0, true>(T, W) : pick_w<kQ4_0, false>(T, W);
+    return h ? pick_w<kQ4_1, true>(T, W) : pick_w<kQ4_1, false>(T, W);
 }
 
 // Weight-tile widths a call may use: 64, 128, 160 and (one token tile) 224
@@ -689,10 +738,15 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     }
     GArgs a;
     const int row_bytes = (K / QK) * block_bytes(qt);
-    cudaError_t e = encode_map_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, (uint64_t)K, (uint64_t)M,
-                                  (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (e != cudaSuccess) return e;
     const GemmPlan gp = gemm_plan(qt, M, N, K);
+    // one token tile of fewer than 128 rows: boxes of the real rows only (the
+    // kernel keeps the rest of each stage zero); out-of-range boxes would move
+    // 128 rows of zero fill per K step
+    const bool half = gp.T == 1 && M <= 64;  // MMA M = 64 token tiles
+    a.xrows = gp.T == 1 && M < BM ? (M + 7) / 8 * 8 : BM;
+    cudaError_t e = encode_map_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, (uint64_t)K, (uint64_t)M,
+                                  (uint64_t)K * 2, BK, (uint32_t)a.xrows, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e != cudaSuccess) return e;
     const int T = gp.T, W = gp.W;
     const long tiles = (long)((N + W - 1) / W) * ((M + T * BM - 1) / (T * BM));
     a.ks = gp.ks;
@@ -720,8 +774,8 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     a.gact = g.act;
     a.gout = g.out;
     a.ghidden = g.hidden;
-    const void* fn = gemm_kernel_for(qt, T, W);
-    const size_t smem = gemm_smem_bytes(qt, T, W);
+    const void* fn = gemm_kernel_for(qt, T, W, half);
+    const size_t smem = gemm_smem_bytes(qt, T, W, half);
     e = ensure_dynamic_smem(fn, smem);
     if (e != cudaSuccess) return e;
     void* args[] = {(void*)&a};

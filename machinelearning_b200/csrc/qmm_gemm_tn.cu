@@ -2,8 +2,9 @@
 // split stacked into a single MMA, stream-K schedule.
 //
 // y[M, N] = x[M, K] . W[N, K]^T for f32 activations and GGUF block weights
-// (Q4_0 / Q4_1 / Q8_0 rows, raw bytes) when M is a decode batch (kGemmMinRows
-// .. kGemmTnMaxRows tokens). Replaces the M > 4 row-parallel CPU loops of
+// (Q4_0 / Q4_1 / Q8_0 rows, raw bytes) when M is a decode batch of 33 ..
+// kGemmTnMaxRows tokens, or 17 .. 32 tokens whose row pitch the prefill GEMM
+// cannot take (8 mod 16 bytes). Replaces the M > 4 row-parallel CPU loops of
 // matmul_f32_q4 / _q8 / _q4_1 (reference llmserve/llmmodel/kernel/main/src/
 // core/quantize.rs:317-395, 557-630, 807-932) for batched decode.
 //

@@ -1,39 +1,44 @@
-// Prefill GEMM for sm_100a: tcgen05 tensor cores with TMEM accumulators.
+// f16 tensor-core GEMM for sm_100a (prefill and decode batches): tcgen05 with
+// TMEM accumulators.
 //
 // y[M, N] = x[M, K] . W[N, K]^T for f32 activations and GGUF block weights
 // (Q4_0 / Q4_1 / Q8_0 rows, raw bytes), M >= kGemmMinRows. Replaces the M > 4
 // row-parallel CPU loops of matmul_f32_q4 / _q8 / _q4_1 (reference
 // llmserve/llmmodel/kernel/main/src/core/quantize.rs:317-395, 557-630,
-// 807-932) for prefill-sized M.
+// 807-932).
 //
 // Two launches per call:
 //   1. gemm_xprep: each activation row is scaled by a power of two (its max
-//      lands in [2^14, 2^15)) and rounded to f16; the scale is kept per row.
-//   2. gemm_kernel<QT, T>: one CTA per output tile of T x 128 tokens by 128
-//      weight rows, full K, eleven warps:
-//        warp 0    TMA producer of T x16 tiles [128 tokens x 64] per K step
-//                  with 128-byte swizzle (the canonical K-major UMMA layout);
-//        warp 10   TMA producer of raw weight chunks [128 rows x 8 blocks]
-//                  (2-D boxes of the GGUF bytes);
-//        warp 1    allocates T x 128 TMEM columns; one thread issues
-//                  tcgen05.mma.kind::f16 (M 128, N 128, K 16, both operands
-//                  read from shared memory through descriptors) into T
-//                  accumulators and commits to mbarriers;
-//        warps 2-9 dequantise: each thread one 32-weight block of one row per
+//      lands in [2^14, 2^15)) and rounded to f16; up to 128 tokens the f16
+//      residual of every row is written too, as the rows M .. 2M - 1 of the
+//      same token tile (exact activations: D rows m and M + m add).
+//   2. gemm_kernel<QT, T, W, H, P>: one CTA per output tile of the token tile
+//      (T x 128 rows, or 64 when H: MMA M = 64 for up to 64 stacked rows) by
+//      W weight rows (64 .. 224), full K or a K slice:
+//        warp 0    TMA producer of the x16 tiles [rows x 64] per K step with
+//                  128-byte swizzle (the canonical K-major UMMA layout); the
+//                  boxes carry the real rows only, the rest stays zero;
+//        last warp TMA producer of raw weight chunks [W rows x 8 blocks]: one
+//                  2-D box of the GGUF bytes, or (P: 8-mod-16 row pitches) two
+//                  boxes of the paired view [N/2][2 * row_bytes];
+//        warp 1    allocates TMEM; one thread issues tcgen05.mma.kind::f16
+//                  (M 128 or 64, N W, K 16, both operands read from shared
+//                  memory through descriptors) and commits to mbarriers;
+//        warps 2.. dequantise: each thread one 32-weight block of one row per
 //                  K step (magic-number f16 pairs, one f16 rounding of d*q,
 //                  d*(n-8) or d*n+m), written into the swizzled B tile; then
-//                  they read the accumulators back with tcgen05.ld (two warps
-//                  per TMEM lane quarter) into a staging tile and write
-//                  y = acc * row scale as whole coalesced rows.
-//      One dequantised B tile feeds T accumulators: T = 2 for M > 128 halves
-//      the dequantisation per flop. Rings: x16 tiles 6 (T = 1) or 3-4 (T = 2)
-//      stages, weight tiles 3, raw chunks 2; every wait is bounded (error word
-//      on timeout, in-flight copies drained before exit).
+//                  they read the accumulators back with tcgen05.ld into a
+//                  staging tile (weight-row order) and write y = acc * row
+//                  scale as whole coalesced rows, or the gate/up activation.
+//      One dequantised B tile feeds T accumulators: T = 2 for more than 128
+//      rows halves the dequantisation per flop. Every wait is bounded (error
+//      word on timeout, in-flight copies drained before exit).
 //
-// Numerics: both operands are rounded to f16 (unit roundoff 2^-11), products
-// are exact and accumulate in f32: relative error ~3e-4 of ||y|| on N(0, 1)
-// activations, inside the 1e-3 contract (the GEMV paths carry activations as
-// f16 hi+lo and stay near 1e-5).
+// Numerics: d*q is rounded to f16 once (unit roundoff 2^-11), products are
+// exact and accumulate in f32. Up to 128 tokens the activations are exact
+// (hi + residual): ~2e-4 of ||y||; above, they are rounded to f16 too: ~3e-4
+// on N(0, 1) activations; both inside the 1e-3 contract (the GEMV paths carry
+// activations as f16 hi+lo and exact weights and stay near 1e-5).
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -77,6 +82,14 @@ __host__ __device__ constexpr int b_stages(int qt, int, int W = BN) { return (qt
 // blocks, padded so consecutive rows sit an odd number of 16-byte units apart
 // (conflict-free 16-byte loads by consecutive threads).
 __host__ __device__ constexpr int raw_pitch(int qt) { return qt == kQ8_0 ? 272 : (qt == kQ4_0 ? 144 : 176); }
+// Row pitches of 8 mod 16 bytes (K = 1152: 648-byte Q4_0 / 1224-byte Q8_0
+// rows) are read through a paired view of the weights, [N/2][2 * row_bytes]
+// (16-byte pitched): per chunk one box of the even rows and one of the odd
+// rows starting 8 bytes early, so no padded copy is needed. The stage holds
+// the even rows, then the odd rows (8 bytes of skew each: a wider pitch).
+__host__ __device__ constexpr int raw_pitch_p(int qt, bool p) {
+    return p ? (qt == kQ8_0 ? 304 : (qt == kQ4_0 ? 176 : 208)) : raw_pitch(qt);
+}
 
 struct GArgs {
     CUtensorMap tmap_x;  // x16 [M][K] f16, box [64, 128], 128-byte swizzle
@@ -84,7 +97,9 @@ struct GArgs {
     const float* xs;     // per-row activation scales
     float* y;
     int M, N, K, ksteps, weights_immutable;
-    int xrows;           // token rows one x16 box carries (T == 1: M rounded up to 8; else BM)
+    int xrows;           // token rows one x16 box carries (T == 1: rows rounded up to 8; else BM)
+    int stack;           // x16 rows [M, 2M) are the f16 residuals of rows [0, M): D rows r and M + r add
+    int nb, row_bytes;   // blocks and bytes per weight row
     int* err;
     int ks, cps;         // K slices (blockIdx.z) and raw chunks per slice
     float* partial;      // [ks][M][N] unscaled partial tiles (ks > 1)
@@ -103,21 +118,21 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 // the 32-token lm_head from 366 to 339 us on B200.
 __host__ __device__ constexpr int x_stages(int qt, int T, int W, bool h) { return (h ? 2 : 1) * a_stages(qt, T, W); }
 __host__ __device__ constexpr uint32_t x_tile_bytes(bool h) { return (h ? 64u : (uint32_t)BM) * BK * 2; }
-__host__ __device__ constexpr size_t gemm_smem_with(int qt, int T, int W, int sr, bool h) {
+__host__ __device__ constexpr size_t gemm_smem_with(int qt, int T, int W, int sr, bool h, bool p = false) {
     return 1024 + (size_t)x_stages(qt, T, W, h) * T * x_tile_bytes(h) + (size_t)b_stages(qt, T, W) * W * BK * 2 +
-           (size_t)sr * W * raw_pitch(qt) + (2 * x_stages(qt, T, W, h) + 2 * b_stages(qt, T, W) + 2 * sr + 1) * 8 +
-           16;
+           (size_t)sr * W * raw_pitch_p(qt, p) +
+           (2 * x_stages(qt, T, W, h) + 2 * b_stages(qt, T, W) + 2 * sr + 1) * 8 + 16;
 }
 // Raw chunk stages: as many as fit (2..6). A chunk is 4 K steps and its TMA
 // load takes ~2 us to land under load; the narrower tiles have room to keep
 // more of them in flight.
-__host__ __device__ constexpr int raw_stages(int qt, int T, int W, bool h = false) {
+__host__ __device__ constexpr int raw_stages(int qt, int T, int W, bool h = false, bool p = false) {
     int sr = 6;
-    while (sr > 2 && gemm_smem_with(qt, T, W, sr, h) > 232448) --sr;
+    while (sr > 2 && gemm_smem_with(qt, T, W, sr, h, p) > 232448) --sr;
     return sr;
 }
-__host__ __device__ constexpr size_t gemm_smem_bytes(int qt, int T, int W, bool h = false) {
-    return gemm_smem_with(qt, T, W, raw_stages(qt, T, W, h), h);
+__host__ __device__ constexpr size_t gemm_smem_bytes(int qt, int T, int W, bool h = false, bool p = false) {
+    return gemm_smem_with(qt, T, W, raw_stages(qt, T, W, h, p), h, p);
 }
 static_assert(gemm_smem_bytes(kQ4_0, 2, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 2, 160) <= 232448 &&
                   gemm_smem_bytes(kQ4_0, 1, 160) <= 232448 && gemm_smem_bytes(kQ4_1, 1, 160) <= 232448 &&
@@ -208,15 +223,23 @@ __device__ __forceinline__ void dequant_block(const uint8_t* row, uint8_t* dst, 
     for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(dst + (((CB + i) ^ r7) << 4)) = c[i];
 }
 
-// Block BLK (0 or 1) of K step KK of a raw chunk.
-template <int QT, int KK, int BLK>
+// Block BLK (0 or 1) of K step KK of a raw chunk whose row starts SK bytes
+// into its shared-memory row (8 for the paired view's odd rows).
+template <int QT, int KK, int BLK, int SK = 0>
 __device__ __forceinline__ void dequant_kstep(const uint8_t* row, uint8_t* dst, int r7) {
-    dequant_block<QT, block_bytes(QT) * (2 * KK + BLK), 4 * BLK>(row, dst, r7);
+    dequant_block<QT, SK + block_bytes(QT) * (2 * KK + BLK), 4 * BLK>(row, dst, r7);
+}
+// Zero weights for a block past the row end (the paired view's boxes bring
+// the neighbouring row's bytes there, not zero fill).
+template <int BLK>
+__device__ __forceinline__ void zero_kstep(uint8_t* dst, int r7) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(dst + (((4 * BLK + i) ^ r7) << 4)) = make_uint4(0, 0, 0, 0);
 }
 
 // ---- activation prep: x f32 -> x16 f16 with a power-of-two scale per row ---------------
 __global__ void gemm_xprep_kernel(const float* __restrict__ x, int M, int K, __half* __restrict__ x16,
-                                  float* __restrict__ xs) {
+                                  float* __restrict__ xs, int stack) {
     pdl_launch_dependents();
     pdl_wait();  // x comes from the preceding work in the stream
     __shared__ float red[32];
@@ -264,31 +287,47 @@ __global__ void gemm_xprep_kernel(const float* __restrict__ x, int M, int K, __h
     }
     const float scale = (-e >= -126) ? __int_as_float((127 - e) << 23) : __int_as_float(0x00400000);
     __half* out = x16 + (int64_t)m * K;
+    // stacked: row M + m holds the f16 residual (exact in f32, then rounded:
+    // hi + lo carries ~22 significant bits)
+    __half* lo = stack ? x16 + (int64_t)(M + m) * K : nullptr;
     if (v4) {
         uint2* o2 = reinterpret_cast<uint2*>(out);  // 4 halves per float4 (rows are 64-byte multiples)
+        uint2* l2 = reinterpret_cast<uint2*>(lo);
         for (int k = threadIdx.x; k < n4; k += blockDim.x) {
             const float4 v = r4[k];
-            const __half2 h01 = __floats2half2_rn(v.x * scale, v.y * scale);
-            const __half2 h23 = __floats2half2_rn(v.z * scale, v.w * scale);
+            const float a0 = v.x * scale, a1 = v.y * scale, a2 = v.z * scale, a3 = v.w * scale;
+            const __half2 h01 = __floats2half2_rn(a0, a1);
+            const __half2 h23 = __floats2half2_rn(a2, a3);
             o2[k] = make_uint2(h2_u32(h01), h2_u32(h23));
+            if (stack) {
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                l2[k] = make_uint2(h2_u32(__floats2half2_rn(a0 - f01.x, a1 - f01.y)),
+                                   h2_u32(__floats2half2_rn(a2 - f23.x, a3 - f23.y)));
+            }
         }
     } else {
-        for (int k = threadIdx.x; k < K; k += blockDim.x) out[k] = __float2half_rn(row[k] * scale);
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            const float a0 = row[k] * scale;
+            const __half h = __float2half_rn(a0);
+            out[k] = h;
+            if (stack) lo[k] = __float2half_rn(a0 - __half2float(h));
+        }
     }
     if (threadIdx.x == 0) xs[m] = __int_as_float((e + 127) << 23);
 }
 
-template <int QT, int T, int W, bool H>
+template <int QT, int T, int W, bool H, bool P>
 __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_constant__ GArgs a) {
     static_assert(!H || T == 1, "half-height token tiles come one per CTA");
+    static_assert(!P || (T == 1 && W % 64 == 0), "paired view: one token tile, even and odd halves of whole warps");
     constexpr int BMk = H ? 64 : BM;                 // MMA M (token rows of a tile)
     constexpr uint32_t kATile = x_tile_bytes(H);     // x16 stage bytes per token tile
     constexpr int SA = x_stages(QT, T, W, H), SB = b_stages(QT, T, W);
     constexpr int kDqWarps = dq_warps(W), kDqThreads = dq_threads(W);
     constexpr uint32_t kBTile = (uint32_t)W * BK * 2;  // dequantised weight tile bytes
     constexpr uint32_t kTmemCols = T * W <= 128 ? 128 : (T * W <= 256 ? 256 : 512);
-    constexpr int PITCH = raw_pitch(QT);
-    constexpr int SR = raw_stages(QT, T, W, H);
+    constexpr int PITCH = raw_pitch_p(QT, P);
+    constexpr int SR = raw_stages(QT, T, W, H, P);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                        // [SA][T] x16 tiles
@@ -391,8 +430,17 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
             int r_issued = 0;
             auto issue_raw = [&](int ci) {  // the ci-th chunk of this CTA's sequence
                 const int sr = ci % SR;
+                const int cb = chunk_of(ci) * 8 * block_bytes(QT);  // byte offset of the chunk in a row
                 mbar_arrive_expect_tx(&rfull[sr], (uint32_t)(W * PITCH));
-                tma_load_2d(sR + sr * W * PITCH, &a.tmap_w, chunk_of(ci) * 8 * block_bytes(QT) / 4, n0, &rfull[sr]);
+                if constexpr (P) {
+                    // even rows 2p at [p][cb]; odd rows 2p + 1 from 8 bytes before
+                    // their chunk, [p][row_bytes + cb - 8] (16-byte aligned)
+                    tma_load_2d(sR + sr * W * PITCH, &a.tmap_w, cb / 4, n0 / 2, &rfull[sr]);
+                    tma_load_2d(sR + sr * W * PITCH + (W / 2) * PITCH, &a.tmap_w, (a.row_bytes + cb - 8) / 4, n0 / 2,
+                                &rfull[sr]);
+                } else {
+                    tma_load_2d(sR + sr * W * PITCH, &a.tmap_w, cb / 4, n0, &rfull[sr]);
+                }
             };
             // immutable weights: the first chunks may load before the dependency wait
             if (a.weights_immutable)
@@ -439,16 +487,25 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         const int r7 = row & 7;
         pdl_wait();
         bool ok = true;
-        auto step = [&](int i, int sr, auto kk) {  // operand step i, K step KK of raw stage sr
+        // paired view: tile rows [W/2, W) are the odd weight rows, 8 bytes
+        // into their shared rows (warp-uniform: W/2 is a multiple of 32)
+        const bool skew = P && row >= W / 2;
+        auto step = [&](int i, int sr, int chunk, auto kk) {  // operand step i, K step KK of raw stage sr
             constexpr int KK = decltype(kk)::value;
             const int s = i % SB;
             if (i >= SB && !mbar_wait_bounded(&empty_b[s], ((i / SB) - 1) & 1, a.err)) return false;
             const uint8_t* rrow = sR + sr * W * PITCH + row * PITCH;
             uint8_t* dst = sB + s * kBTile + (row >> 3) * 1024 + r7 * 128;
-            if (blk == 0)
-                dequant_kstep<QT, KK, 0>(rrow, dst, r7);
-            else
-                dequant_kstep<QT, KK, 1>(rrow, dst, r7);
+            if (P && chunk * 8 + 2 * KK + blk >= a.nb) {
+                if (blk == 0) zero_kstep<0>(dst, r7);
+                else zero_kstep<1>(dst, r7);
+            } else if (skew) {
+                if (blk == 0) dequant_kstep<QT, KK, 0, 8>(rrow, dst, r7);
+                else dequant_kstep<QT, KK, 1, 8>(rrow, dst, r7);
+            } else {
+                if (blk == 0) dequant_kstep<QT, KK, 0>(rrow, dst, r7);
+                else dequant_kstep<QT, KK, 1>(rrow, dst, r7);
+            }
             fence_proxy_async_smem();  // generic writes -> visible to the tensor core
             mbar_arrive(&full_b[s]);
             return true;
@@ -457,11 +514,12 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         for (int ci = 0; ci < nchunks && ok; ++ci) {
             const int sr = ci % SR;
             if (!mbar_wait_bounded(&rfull[sr], (ci / SR) & 1, a.err)) break;
-            const int nk = min(kStepsPerChunk, a.ksteps - chunk_of(ci) * kStepsPerChunk);
-            ok = step(i, sr, std::integral_constant<int, 0>{});
-            if (ok && nk > 1) ok = step(i + 1, sr, std::integral_constant<int, 1>{});
-            if (ok && nk > 2) ok = step(i + 2, sr, std::integral_constant<int, 2>{});
-            if (ok && nk > 3) ok = step(i + 3, sr, std::integral_constant<int, 3>{});
+            const int chunk = chunk_of(ci);
+            const int nk = min(kStepsPerChunk, a.ksteps - chunk * kStepsPerChunk);
+            ok = step(i, sr, chunk, std::integral_constant<int, 0>{});
+            if (ok && nk > 1) ok = step(i + 1, sr, chunk, std::integral_constant<int, 1>{});
+            if (ok && nk > 2) ok = step(i + 2, sr, chunk, std::integral_constant<int, 2>{});
+            if (ok && nk > 3) ok = step(i + 3, sr, chunk, std::integral_constant<int, 3>{});
             i += nk;
             mbar_arrive(&rempty[sr]);  // the chunk is consumed
         }
@@ -487,16 +545,36 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
                 uint32_t v[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * W + cb * 32), v);
                 float4* dstp = reinterpret_cast<float4*>(ys + r * YP + cb * 32);
-                if (holds) {
+                if (holds && !P) {
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
                         dstp[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
                                               __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+                } else if (holds) {
+                    // paired view: accumulator column c is weight row 2c (c < W/2)
+                    // or 2 (c - W/2) + 1; staged in weight-row order
+                    const int c0 = cb * 32;  // all 32 columns in one half (W/2 % 32 == 0)
+                    const int base = c0 < W / 2 ? 2 * c0 : 2 * (c0 - W / 2) + 1;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) ys[r * YP + base + 2 * j] = __uint_as_float(v[j]);
                 }
             }
         }
         tc_fence_before();
         asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");  // the staging tile is complete
+        if (a.stack) {
+            // stacked activations: token m's products with its hi row (r = m)
+            // and its lo row (r = M + m) add
+            const int w4 = W / 4;
+            for (int idx = threadIdx.x - 64; idx < a.M * w4; idx += kDqThreads) {
+                const int r = idx / w4, c4 = idx - r * w4;
+                float4* ph = reinterpret_cast<float4*>(ys + r * YP) + c4;
+                const float4 l = *(reinterpret_cast<const float4*>(ys + (r + a.M) * YP) + c4);
+                const float4 h = *ph;
+                *ph = make_float4(h.x + l.x, h.y + l.y, h.z + l.z, h.w + l.w);
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kDqThreads) : "memory");
+        }
         bool store = acc_ok;
         if (a.ks > 1) {
             // K split: this slice's unscaled tile to the workspace; the last slice
@@ -599,34 +677,41 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
 }
 
 template <int QT, bool H>
-const void* pick_w(int T, int W) {
+const void* pick_w(int T, int W, bool p) {
     if constexpr (H) {
-        if (W == 64) return (const void*)gemm_kernel<QT, 1, 64, true>;
-        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224, true>;
+        if (p) return W == 64 ? (const void*)gemm_kernel<QT, 1, 64, true, true> : (const void*)gemm_kernel<QT, 1, BN, true, true>;
+        if (W == 64) return (const void*)gemm_kernel<QT, 1, 64, true, false>;
+        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224, true, false>;
         if constexpr (QT != kQ8_0) {
-            if (W == 160) return (const void*)gemm_kernel<QT, 1, 160, true>;
+            if (W == 160) return (const void*)gemm_kernel<QT, 1, 160, true, false>;
         }
-        return (const void*)gemm_kernel<QT, 1, BN, true>;
+        return (const void*)gemm_kernel<QT, 1, BN, true, false>;
     } else {
-        if (W == 64) return T == 1 ? (const void*)gemm_kernel<QT, 1, 64, false> : (const void*)gemm_kernel<QT, 2, 64, false>;
-        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224, false>;
+        if (p) return W == 64 ? (const void*)gemm_kernel<QT, 1, 64, false, true> : (const void*)gemm_kernel<QT, 1, BN, false, true>;
+        if (W == 64)
+            return T == 1 ? (const void*)gemm_kernel<QT, 1, 64, false, false> : (const void*)gemm_kernel<QT, 2, 64, false, false>;
+        if (W == 224) return (const void*)gemm_kernel<QT, 1, 224, false, false>;
         if constexpr (QT != kQ8_0) {
             if (W == 160)
-                return T == 1 ? (const void*)gemm_kernel<QT, 1, 160, false> : (const void*)gemm_kernel<QT, 2, 160, false>;
+                return T == 1 ? (const void*)gemm_kernel<QT, 1, 160, false, false>
+                              : (const void*)gemm_kernel<QT, 2, 160, false, false>;
         }
-        return T == 1 ? (const void*)gemm_kernel<QT, 1, BN, false> : (const void*)gemm_kernel<QT, 2, BN, false>;
+        return T == 1 ? (const void*)gemm_kernel<QT, 1, BN, false, false> : (const void*)gemm_kernel<QT, 2, BN, false, false>;
     }
 }
-const void* gemm_kernel_for(int qt, int T, int W, bool h) {
-    if (qt == kQ8_0) return h ? pick_w<kQ8_0, true>(T, W) : pick_w<kQ8_0, false>(T, W);
-    if (qt == kQ4_0) return h ? pick_w<kQ4_0, true>(T, W) : pick_w<kQ4_0, false>(T, W);
-    return h ? pick_w<kQ4_1, true>(T, W) : pick_w<kQ4_1, false>(T, W);
+const void* gemm_kernel_for(int qt, int T, int W, bool h, bool p) {
+    if (qt == kQ8_0) return h ? pick_w<kQ8_0, true>(T, W, p) : pick_w<kQ8_0, false>(T, W, p);
+    if (qt == kQ4_0) return h ? pick_w<kQ4_0, true>(T, W, p) : pick_w<kQ4_0, false>(T, W, p);
+    return h ? pick_w<kQ4_1, true>(T, W, p) : pick_w<kQ4_1, false>(T, W, p);
 }
 
 // Weight-tile widths a call may use: 64, 128, 160 and (one token tile) 224
 // rows for Q4_0 / Q4_1; 64, 128 and (one token tile, shallower rings) 224 for
 // Q8_0 (its raw chunks are twice as wide).
-bool gemm_width_ok(int qt, int T, int W) {
+// The paired view (8-mod-16 row pitches) takes one token tile and 64 or 128
+// rows (its halves must be whole warps of dequantisers).
+bool gemm_width_ok(int qt, int T, int W, bool paired = false) {
+    if (paired) return T == 1 && (W == 64 || W == BN);
     if (W == 64 || W == BN || (W == 224 && T == 1)) return true;
     return qt != kQ8_0 && W == 160;
 }
@@ -649,17 +734,27 @@ cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 }  // namespace
 
 namespace {
-// Shapes the prefill GEMM below can run: 2-D TMA boxes of the raw rows need a
-// row pitch that is a multiple of 16 bytes.
+
+// Decode batches (M <= 128) carry their activations exactly: f16 hi rows and
+// f16 residual rows stacked in one token tile (2M MMA rows: the half-height
+// tile up to 32 tokens, one or two full tiles up to 128), so only the weights'
+// f16 rounding of d*q remains (~2e-4 norm-wise instead of ~3e-4). Larger M
+// (prefill, tensor-bound) rounds the activations once.
+int x_rows(int M) { return M <= 128 ? 2 * M : M; }
+bool paired_pitch(int qt, int K) { return ((int64_t)(K / QK) * block_bytes(qt)) % 16 == 8; }
+// Shapes the GEMM below can run: 2-D TMA boxes of the raw rows need a row
+// pitch that is a multiple of 16 bytes, or 8 mod 16 through the paired view
+// (N even, one token tile: up to 64 tokens).
 bool single_shape_ok(int qt, int M, int N, int K) {
     if (M < kGemmMinRows || N < 1 || K < QK || K % QK) return false;
     const int bb = block_bytes(qt);
-    return bb && ((int64_t)(K / QK) * bb) % 16 == 0;
+    if (!bb) return false;
+    const int64_t rb = (int64_t)(K / QK) * bb;
+    if (rb % 16 == 0) return true;
+    return rb % 16 == 8 && N % 2 == 0 && x_rows(M) <= BM;
 }
-// Decode batches of 33..kGemmTnMaxRows tokens run on the decode-batch GEMM
-// (qmm_gemm_tn.cu, exact operand split, 8-mod-16 row pitches too), and so do
-// 17..32 tokens where the prefill GEMM cannot take the row pitch; the rest on
-// the prefill GEMM below.
+// The decode-batch GEMM (qmm_gemm_tn.cu, exact operand split) takes the decode
+// batches this GEMM cannot: 8-mod-16 pitches with odd N or 65..128 tokens.
 bool route_tn(int qt, int M, int N, int K) {
     if (!gemm_tn_supported(qt, false, M, N, K)) return false;
     return M > kGemmSingleMaxRows || !single_shape_ok(qt, M, N, K);
@@ -682,7 +777,7 @@ namespace {
 struct GemmPlan {
     int T, W, ks, cps;
 };
-GemmPlan gemm_plan(int qt, int M, int N, int K) {
+GemmPlan gemm_plan(int qt, int M, int N, int K, bool paired = false) {
     GemmPlan p{M > BM ? 2 : 1, BN, 1, 0};
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -692,7 +787,7 @@ GemmPlan gemm_plan(int qt, int M, int N, int K) {
     const long gy = (M + p.T * BM - 1) / (p.T * BM);
     double best = -1.0;
     for (const int w : {64, 128, 160, 224}) {
-        if (!gemm_width_ok(qt, p.T, w)) continue;
+        if (!gemm_width_ok(qt, p.T, w, paired)) continue;
         for (int ks = 1; ks <= 4; ks *= 2) {
             const int cps = (nch + ks - 1) / ks;
             if ((nch + cps - 1) / cps != ks) continue;  // every slice gets a chunk
@@ -712,13 +807,16 @@ GemmPlan gemm_plan(int qt, int M, int N, int K) {
 size_t x16_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((size_t)M * 4); }
 }  // namespace
 
+
+
 size_t gemm_workspace_bytes(int M, int N, int K, int qt, bool native) {
     if (native) return gemm_i8_workspace_bytes(M, N, K, qt);
     if (route_tn(qt, M, N, K)) return gemm_tn_workspace_bytes(M, N, K, qt);
-    const GemmPlan p = gemm_plan(qt, M, N, K);
-    size_t b = x16_bytes(M, K);
+    const int R = x_rows(M);
+    const GemmPlan p = gemm_plan(qt, R, N, K, paired_pitch(qt, K));
+    size_t b = x16_bytes(R, K);
     if (p.ks > 1) {
-        const long tiles = (long)((N + p.W - 1) / p.W) * ((M + p.T * BM - 1) / (p.T * BM));
+        const long tiles = (long)((N + p.W - 1) / p.W) * ((R + p.T * BM - 1) / (p.T * BM));
         b += align256((size_t)p.ks * M * N * 4) + align256((size_t)tiles * 4);
     }
     return b;
@@ -729,39 +827,48 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     if (native) return launch_gemm_i8(qt, w, x, y, M, N, K, ws, err, st, weights_immutable);
     if (route_tn(qt, M, N, K))
         return launch_gemm_tn(qt, w, x, y, M, N, K, ws, err, st, weights_immutable, g);
+    const int R = x_rows(M);  // x16 rows: hi rows, then (M <= 128) the residual rows
+    int stack = R != M ? 1 : 0;
     __half* x16 = static_cast<__half*>(ws);
-    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256((size_t)M * K * 2));
+    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256((size_t)R * K * 2));
     {
-        void* args[] = {(void*)&x, (void*)&M, (void*)&K, (void*)&x16, (void*)&xs};
+        void* args[] = {(void*)&x, (void*)&M, (void*)&K, (void*)&x16, (void*)&xs, (void*)&stack};
         cudaError_t e = launch_ex((const void*)gemm_xprep_kernel, dim3(M), dim3(256), 0, st, args);
         if (e != cudaSuccess) return e;
     }
     GArgs a;
     const int row_bytes = (K / QK) * block_bytes(qt);
-    const GemmPlan gp = gemm_plan(qt, M, N, K);
+    const bool paired = paired_pitch(qt, K);
+    const GemmPlan gp = gemm_plan(qt, R, N, K, paired);
     // one token tile of fewer than 128 rows: boxes of the real rows only (the
     // kernel keeps the rest of each stage zero); out-of-range boxes would move
     // 128 rows of zero fill per K step
-    const bool half = gp.T == 1 && M <= 64;  // MMA M = 64 token tiles
-    a.xrows = gp.T == 1 && M < BM ? (M + 7) / 8 * 8 : BM;
-    cudaError_t e = encode_map_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, (uint64_t)K, (uint64_t)M,
+    const bool half = gp.T == 1 && R <= 64;  // MMA M = 64 token tiles
+    a.xrows = gp.T == 1 && R < BM ? (R + 7) / 8 * 8 : BM;
+    a.stack = stack;
+    cudaError_t e = encode_map_2d(&a.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, (uint64_t)K, (uint64_t)R,
                                   (uint64_t)K * 2, BK, (uint32_t)a.xrows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
     const int T = gp.T, W = gp.W;
-    const long tiles = (long)((N + W - 1) / W) * ((M + T * BM - 1) / (T * BM));
+    const long tiles = (long)((N + W - 1) / W) * ((R + T * BM - 1) / (T * BM));
     a.ks = gp.ks;
     a.cps = gp.cps;
     a.partial = nullptr;
     a.counters = nullptr;
     if (gp.ks > 1) {
-        uint8_t* b = static_cast<uint8_t*>(ws) + x16_bytes(M, K);
+        uint8_t* b = static_cast<uint8_t*>(ws) + x16_bytes(R, K);
         a.partial = reinterpret_cast<float*>(b);
         a.counters = reinterpret_cast<unsigned*>(b + align256((size_t)gp.ks * M * N * 4));
         e = cudaMemsetAsync(a.counters, 0, (size_t)tiles * 4, st);  // the tickets start from zero
         if (e != cudaSuccess) return e;
     }
-    e = encode_map_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, (uint64_t)row_bytes / 4, (uint64_t)N,
-                      (uint64_t)row_bytes, (uint32_t)raw_pitch(qt) / 4, (uint32_t)W, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (paired)  // [N/2][2 * row_bytes]: rows 2p and 2p + 1 side by side, 16-byte pitched
+        e = encode_map_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, (uint64_t)row_bytes / 2, (uint64_t)N / 2,
+                          (uint64_t)row_bytes * 2, (uint32_t)raw_pitch_p(qt, true) / 4, (uint32_t)W / 2,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+    else
+        e = encode_map_2d(&a.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, (uint64_t)row_bytes / 4, (uint64_t)N,
+                          (uint64_t)row_bytes, (uint32_t)raw_pitch(qt) / 4, (uint32_t)W, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (e != cudaSuccess) return e;
     a.xs = xs;
     a.y = y;
@@ -774,12 +881,14 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     a.gact = g.act;
     a.gout = g.out;
     a.ghidden = g.hidden;
-    const void* fn = gemm_kernel_for(qt, T, W, half);
-    const size_t smem = gemm_smem_bytes(qt, T, W, half);
+    a.nb = K / QK;
+    a.row_bytes = row_bytes;
+    const void* fn = gemm_kernel_for(qt, T, W, half, paired);
+    const size_t smem = gemm_smem_bytes(qt, T, W, half, paired);
     e = ensure_dynamic_smem(fn, smem);
     if (e != cudaSuccess) return e;
     void* args[] = {(void*)&a};
-    return launch_ex(fn, dim3((N + W - 1) / W, (M + T * BM - 1) / (T * BM), gp.ks), dim3(gemm_threads(W)), smem,
+    return launch_ex(fn, dim3((N + W - 1) / W, (R + T * BM - 1) / (T * BM), gp.ks), dim3(gemm_threads(W)), smem,
                      st, args);
 }
 

@@ -2,9 +2,10 @@
 // split stacked into a single MMA, stream-K schedule.
 //
 // y[M, N] = x[M, K] . W[N, K]^T for f32 activations and GGUF block weights
-// (Q4_0 / Q4_1 / Q8_0 rows, raw bytes) when M is a decode batch of 33 ..
-// kGemmTnMaxRows tokens, or 17 .. 32 tokens whose row pitch the prefill GEMM
-// cannot take (8 mod 16 bytes). Replaces the M > 4 row-parallel CPU loops of
+// (Q4_0 / Q4_1 / Q8_0 rows, raw bytes) for the decode batches (17 ..
+// kGemmTnMaxRows tokens) the f16 GEMM of qmm_gemm.cu does not take: row
+// pitches of 8 mod 16 bytes with odd N or more than 64 tokens. Replaces the
+// M > 4 row-parallel CPU loops of
 // matmul_f32_q4 / _q8 / _q4_1 (reference llmserve/llmmodel/kernel/main/src/
 // core/quantize.rs:317-395, 557-630, 807-932) for batched decode.
 //
@@ -15,9 +16,7 @@
 //   activations:  x * 2^-e (a power of two per token row, max in [2^14, 2^15)),
 //                 xh = f16(.), xl = f16(. - xh);
 // and the four products wh.xh + wl.xh + wh.xl + wl.xl accumulate in f32:
-// ~1e-6 relative to the reference's f32 arithmetic, like the GEMV paths. A
-// single f16 rounding per operand (~3e-4 per matmul) compounds past the 1e-3
-// contract over a 26-layer decode step; this does not.
+// ~1e-6 relative to the reference's f32 arithmetic, like the GEMV paths.
 //
 // All four products come from ONE MMA per 16-wide K slice, at the tensor
 // core's full width:

@@ -238,17 +238,18 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
                         int* err, cudaStream_t st, bool weights_immutable, const GatedOut& g = GatedOut(),
                         bool native = false);
 
-// ---- decode-batch GEMM (qmm_gemm_tn.cu): tcgen05, weights on the MMA's M side,
-// tokens on its N side, exact hi/lo split of both operands (~1e-6 relative).
-// f32-activation calls with kGemmMinRows <= M <= kGemmTnMaxRows and a row
-// pitch of 0 or 8 mod 16 bytes (N even for the latter). Calls of at most
-// kGemmSingleMaxRows tokens whose pitch is a multiple of 16 bytes run on the
-// prefill GEMM instead: its single f16 rounding (~3e-4 norm-wise, inside the
-// 1e-3 contract) costs one MMA per K slice where the exact split costs a
-// double-width one, and at 32 tokens the split's fixed per-step cost doubles
-// the call (Llama-70B gate at 32 tokens on B200: 73 us against 164 us).
+// ---- decode-batch GEMM (qmm_gemm_tn.cu): tcgen05, exact hi/lo split of both
+// operands (~1e-6 relative). Capable of f32-activation calls with
+// kGemmMinRows <= M <= kGemmTnMaxRows and a row pitch of 0 or 8 mod 16 bytes
+// (N even for the latter); routed only the decode batches the f16 GEMM
+// (qmm_gemm.cu) cannot take: 8-mod-16 pitches with odd N or more than 64
+// tokens. The f16 GEMM takes every other call of up to kGemmSingleMaxRows
+// tokens: exact activations (f16 hi and residual rows stacked in the token
+// tile) and d*q rounded to f16 once, ~2e-4 norm-wise, at a fraction of the
+// exact split's cost (Gemma decode batch 64 on B200: lm_head 418 -> 226 us,
+// down 152 -> 39 us).
 constexpr int kGemmTnMaxRows = 128;
-constexpr int kGemmSingleMaxRows = 32;
+constexpr int kGemmSingleMaxRows = 128;
 bool gemm_tn_supported(int qt, bool native, int M, int N, int K);
 size_t gemm_tn_workspace_bytes(int M, int N, int K, int qt);
 cudaError_t launch_gemm_tn(int qt, const uint8_t* w, const float* x, float* y, int M, int N, int K, void* ws,

@@ -111,8 +111,13 @@ def test_decode_cache_and_attention_pieces(oracle, torch_cuda):
 # so a step at position p attends over p + 1 entries: p = 0 (one entry), 31 /
 # 32 (either side of a 32-position attention chunk), 511 (the full context,
 # 16 chunks). Batch 1 runs the resident / band GEMVs and the 262144-row padded
-# lm_head, batch 16 the two-token-tile GEMVs, batch 64 the tensor-core GEMM on
-# zero-padded rows.
+# lm_head, batch 16 the two-token-tile GEMVs, batch 64 the f16 tensor-core GEMM
+# on the unpadded K = 1152 rows (paired-row view; exact activations, d*q
+# rounded to f16 once: ~2e-4 norm-wise per matmul). The logits and the cache
+# rows the step writes meet the 1e-3 norm-wise contract at every batch; per
+# element, batch 64's weight rounding compounds over 26 layers (measured up to
+# ~5e-3 of the rms on B200), so its guard is 1e-2 of the rms, as for the other
+# GEMM-path decode test.
 
 @pytest.fixture(scope="module")
 def gemma_1b(torch_cuda, oracle):
@@ -156,10 +161,11 @@ def test_gemma3_1b_decode_at_config_shapes(gemma_1b, torch_cuda, oracle, B, posi
             tokens = rng.integers(0, cfg.vocab, B)
             got = model.step(tokens).cpu().numpy()
             ref = decode_step(cfg, host, tokens, pos, list(kc), list(vc))
-            rel = assert_close_rel(got.ravel(), ref.ravel(), 1e-3)
+            rel = assert_close_rel(got.ravel(), ref.ravel(), 1e-3, 1e-2 if B > 16 else None)
             print(f"batch {B} position {pos}: norm-wise relative error {rel:.2e}")
             # the step wrote the reference's k (normed, rotated) and v at the position
             for dcache, hcache in ((model.k_cache, kc), (model.v_cache, vc)):
-                assert_close_rel(dcache[:, :, :, pos].cpu().numpy().ravel(), hcache[:, :, :, pos].ravel(), 1e-3)
+                assert_close_rel(dcache[:, :, :, pos].cpu().numpy().ravel(), hcache[:, :, :, pos].ravel(), 1e-3,
+                                 1e-2 if B > 16 else None)
     finally:
         model.close()

@@ -63,10 +63,19 @@ def _rows(oracle, dt, n, k, rng, scale=0.05):
     return getattr(oracle, QUANT[dt])(rng.normal(0, scale, n * k).astype(np.float32))
 
 
-def _gemm(dt, m, k):
-    """The prefill GEMM (f16 operands rounded once): M > 128, 16-byte row pitch.
-    Decode batches of 17-128 run the decode-batch GEMM (exact operand split)."""
-    return m > 128 and ((k // 32) * BB[dt]) % 16 == 0
+def _gemm(dt, m, k, n=2):
+    """The f16 tensor-core GEMM (d*q rounded to f16 once): M >= 17 with a
+    16-byte row pitch, or 8 mod 16 with N even and M <= 64 (qmm_gemm.cu:
+    single_shape_ok). Other decode batches run the exact-split GEMM."""
+    rb = (k // 32) * BB[dt]
+    return m >= 17 and (rb % 16 == 0 or (rb % 16 == 8 and n % 2 == 0 and m <= 64))
+
+
+def _gemm_elem(m):
+    """Per-element guard of the f16 GEMM: its errors are Gaussian-tailed
+    (sigma ~2e-4 of the output rms with exact activations, M <= 128; ~4e-4
+    above), so the largest of many outputs reaches ~1e-3 / ~2e-3."""
+    return 2e-3 if m <= 128 else 4e-3
 
 
 def _interleave(gate, up, hidden, k, dt):
@@ -114,7 +123,7 @@ def test_fused_qkv(oracle, dt, k, qd, kvd, m):
     assert out.value == checksum(oracle.fuse_rows(*ws).tobytes())  # byte concatenation, nothing repacked
     x = rng.normal(0, 1, (m, k)).astype(np.float32)
     q, kk, v = proj(torch.from_numpy(x).cuda())
-    er = 4e-3 if _gemm(dt, m, k) else None
+    er = _gemm_elem(m) if _gemm(dt, m, k, qd + 2 * kvd) else None
     for got, w, n in zip((q, kk, v), ws, (qd, kvd, kvd)):
         assert tuple(got.shape) == (m, n) and got.is_contiguous()
         assert_close_rel(got.cpu().numpy(), oracle.MATMUL[(dt, False)](x, w, m, k, n), elem_rtol=er)

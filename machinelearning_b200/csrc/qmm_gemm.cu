@@ -770,7 +770,7 @@ namespace {
 // Launch shape of a call: token tiles per CTA, weight-tile width, K slices and
 // raw chunks per slice. The fewest rounds of CTAs (waves on the SMs) times the
 // K steps a CTA runs times the time per K step, which depends little on the
-// width (measured on B200: ~0.33 + 0.0011 W us per K step for W = 64..224).
+// width (measured on B200: ~0.5 us per K step for W = 64..224 at 32 tokens).
 // Config 3: 138 CTAs of 160 rows (one wave) instead of 172 of 128: 95 ->
 // 52 us; Llama gate at M = 32: 128 CTAs of 224 rows instead of 224 of 128;
 // Llama down at M = 32 (448 K steps): 37 tiles of 224 rows x 4 K slices.
@@ -793,7 +793,10 @@ GemmPlan gemm_plan(int qt, int M, int N, int K, bool paired = false) {
             if ((nch + cps - 1) / cps != ks) continue;  // every slice gets a chunk
             const long rounds = ((N + w - 1) / w * gy * ks + sms - 1) / sms;
             const int steps = min(ksteps, cps * kStepsPerChunk);
-            const double cost = (double)rounds * steps * (300 + w) * (ks > 1 ? 1.03 : 1.0);
+            // a K split also writes and re-reads its partial tiles: measured on
+            // B200, the Llama gate/up weight at 32 tokens ran 198 us split in
+            // four (7 rounds of 32 steps) against ~144 us unsplit (2 rounds of 128)
+            const double cost = (double)rounds * steps * (300 + w) * (ks > 1 ? 1.15 : 1.0);
             if (best < 0.0 || cost < best) {
                 best = cost;
                 p.W = w;

@@ -105,6 +105,12 @@ WORKLOADS = {
         config_index=3, projections=[], batches=[1], copies=1, metric="decode",
         model="Gemma-3-1B architecture, random init: 26 layers, hidden 1152, 4 Q / 1 KV heads of 256, GeGLU 6912, "
               "vocab 262144 tied; linears Q4_0, lm_head Q8_0; KV context 512"),
+    # the same decode step sharded over the N GPUs through the library's NCCL
+    # communicator: FFN Megatron-paired, lm_head by vocabulary rows, attention
+    # replicated (strong scaling: N ranks, one batch)
+    "gemma-decode-tp": dict(
+        config_index=3, projections=[], batches=[1], copies=1, metric="decode",
+        model="Gemma-3-1B architecture as gemma-decode, tensor-parallel over the GPUs"),
     "prefill": dict(
         config_index=2, projections=[("ffn", 4096, 11008, Q4_0, "col")], batches=[512], copies=6,
         model="Llama-7B FFN, Q4_0, 512-token prefill", metric="flops"),
@@ -233,7 +239,7 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-MIN_TIMED_S = 0.1  # every timed region is repeated until the repetitions cover this
+MIN_TIMED_S = 0.25  # every timed region is repeated until the repetitions cover this (>= 20 clock samples)
 
 
 def timed_regions(enqueue, stream, dev, steps, world, sampler, sync=None):
@@ -443,7 +449,7 @@ def run_ours(args, rank, world, local_rank):
     sync()
 
     # timed regions: K steps each, events on the launching stream, max over
-    # ranks, repeated to >= 100 ms, median reported
+    # ranks, repeated to >= MIN_TIMED_S, median reported
     sampler = ClockSampler(local_rank)
     with sampler:
         with torch.cuda.stream(stream):
@@ -778,44 +784,56 @@ def _decode_weights(local_rank, rank):
 
 def run_decode(args, rank, world, local_rank, shared=None):
     """Decode tokens/s of the Gemma-3-1B step (one graph replay per step at
-    position 511, batch args.batch). N > 1: one independent replica per GPU.
-    shared: (cfg, weights) to reuse across batches. Returns rank 0's record."""
+    position 511, batch args.batch). N > 1: one independent replica per GPU
+    (gemma-decode), or one step sharded over the GPUs (gemma-decode-tp: direct
+    launches, the communicator's bounded waits). shared: (cfg, weights) to
+    reuse across batches. Returns rank 0's record."""
     import numpy as np
     import torch
 
     from machinelearning_b200 import _lib
     from machinelearning_b200.decode import Gemma3Decoder
-    cfg, w = shared if shared is not None else _decode_weights(local_rank, rank)
-    model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank)
+    from machinelearning_b200.tp import TpComm
+    tp = args.workload == "gemma-decode-tp" and world > 1
+    # a sharded step needs the same weights on every rank
+    cfg, w = shared if shared is not None else _decode_weights(local_rank, 0 if tp else rank)
+    comm = TpComm.from_group(local_rank, timeout_s=120.0) if tp else None
+    model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank, comm=comm)
     L = _lib.lib()
     dev = model.dev
     B = args.batch
-    rng = np.random.default_rng(5 + rank)
+    rng = np.random.default_rng(5 + (0 if tp else rank))
     model.set_tokens(rng.integers(0, cfg.vocab, B))
     model.set_position(DECODE_POS)
     n0 = L.qmm_launch_count()
     model.step(advance=False)
-    torch.cuda.synchronize(dev)
+    model.wait(120.0)
     launches = int(L.qmm_launch_count() - n0)
     model.capture(advance=False)
     st = model.stream
-    with torch.cuda.stream(st):
-        for _ in range(args.warmup):
-            model.graph.replay()
-    torch.cuda.synchronize(dev)
 
     def enqueue(n):
         for _ in range(n):
-            model.graph.replay()
+            if model.graph is not None:
+                model.graph.replay()
+            else:
+                model._launch(False)
 
+    def sync():
+        model.wait(120.0)
+
+    with torch.cuda.stream(st):
+        enqueue(args.warmup)
+    sync()
     sampler = ClockSampler(local_rank)
     with sampler:
         with torch.cuda.stream(st):
             enqueue(max(args.warmup, 3))
-        torch.cuda.synchronize(dev)
-        ms, regions, n_timed = timed_regions(enqueue, st, dev, args.steps, world, sampler)
+        sync()
+        ms, regions, n_timed = timed_regions(enqueue, st, dev, args.steps, world, sampler, sync)
     ms_per_step = ms / args.steps
-    value = B * world * args.steps / (ms / 1e3)
+    # replicas: every GPU decodes its own batch; sharded: the GPUs decode one
+    value = B * (1 if tp else world) * args.steps / (ms / 1e3)
     step_bytes = decode_bytes(cfg, B, decode_weight_bytes(cfg))
     achieved = step_bytes / (ms_per_step / 1e3) / 1e9
 
@@ -829,18 +847,25 @@ def run_decode(args, rank, world, local_rank, shared=None):
         def e2e_step():
             with torch.cuda.stream(st):
                 model.tokens.copy_(tok_h, non_blocking=True)
-                model.graph.replay()
+                enqueue(1)
                 log_h.copy_(model.logits, non_blocking=True)
-            st.synchronize()
+            sync()
         for _ in range(3):
             e2e_step()
         t0 = time.perf_counter()
         for _ in range(k):
             e2e_step()
         dt_s = time.perf_counter() - t0
-        e2e = {"value": round(B * world * k / dt_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": B * 4,
-               "d2h_bytes_per_step": B * cfg.vocab * 4, "steps": k, "ms_per_step": round(dt_s * 1e3 / k, 4),
-               "path": "pinned host token ids -> graph replay of the decode step -> pinned host logits, synchronous"}
+        if world > 1:  # the slowest rank's clock (the same collective steps on every rank)
+            import torch.distributed as dist
+            t = torch.tensor([dt_s])
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt_s = float(t.item())
+        e2e = {"value": round(B * (1 if tp else world) * k / dt_s, 2), "unit": "tokens/s",
+               "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * cfg.vocab * 4, "steps": k,
+               "ms_per_step": round(dt_s * 1e3 / k, 4),
+               "path": ("pinned host token ids -> the decode step (graph replay; sharded: direct launches and the "
+                        "communicator's wait) -> pinned host logits, synchronous")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -849,20 +874,25 @@ def run_decode(args, rank, world, local_rank, shared=None):
     clocks = sampler.summary()
     clocks["samples_in_timed_region"] = n_timed
     model.close()
+    if comm is not None:
+        _lib.check(comm.close())
     line = None
     if rank == 0:
         line = {
             "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "f32 activations and KV cache x Q4_0 linears / Q8_0 lm_head (f16 tensor-core MMA, f32 accumulate)",
             "data": "synthetic: random-init weights ~N(0,0.02) quantised on device, norm vectors ~N(0,0.1), "
                     "seeded token ids uniform in the vocabulary",
-            "config": {"workload": "gemma-decode", "baseline_config_index": 3,
+            "config": {"workload": args.workload, "baseline_config_index": 3,
                        "model": WORKLOADS["gemma-decode"]["model"],
                        "batch": B, "position": DECODE_POS, "kv_context": cfg.ctx,
-                       "parallelism": f"{world} replicas" if world > 1 else "single",
-                       "graph": "one CUDA graph per step (embedding, 26 layers, final norm, lm_head)",
+                       "parallelism": (f"tp{world}: FFN Megatron-paired, lm_head vocabulary-parallel, attention "
+                                       f"replicated (libqmm NCCL communicator)" if tp else
+                                       (f"{world} replicas" if world > 1 else "single")),
+                       "graph": ("direct launches (sharded step: the non-blocking communicator is not captured)"
+                                 if tp else "one CUDA graph per step (embedding, 26 layers, final norm, lm_head)"),
                        "l2": "weights 0.71 GB > L2", "bytes_per_step": step_bytes},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
@@ -960,7 +990,7 @@ def _init_dist(world, local_rank):
 
 
 def _run_one(args, rank, world, local_rank, shared_decode=None):
-    if args.workload == "gemma-decode":
+    if args.workload in ("gemma-decode", "gemma-decode-tp"):
         return run_decode(args, rank, world, local_rank, shared_decode)
     return run_ours(args, rank, world, local_rank)
 
@@ -992,7 +1022,7 @@ def main(argv=None):
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        if args.workload == "gemma-decode":
+        if args.workload in ("gemma-decode", "gemma-decode-tp"):
             run_decode_reference(args, rank, world)
         else:
             run_reference(args, rank, world)
@@ -1002,16 +1032,19 @@ def main(argv=None):
         line = _run_one(args, rank, world, local_rank)
         if default_run and not args.no_sub:
             # every other BASELINE configuration, timed in this same run (one
-            # GPU); with N GPUs the literal (all-gather) form of the same layer set
+            # GPU); with N GPUs the literal (all-gather) form of the same layer
+            # set and the decode step sharded over the GPUs at batch 1 / 16 / 64
             subs = {}
             shared = None
-            for name, batch in (SUB_WORKLOADS if world == 1 else [("llama70b", None)]):
+            for name, batch in (SUB_WORKLOADS if world == 1 else
+                                [("llama70b", None), ("gemma-decode-tp", 1), ("gemma-decode-tp", 16),
+                                 ("gemma-decode-tp", 64)]):
                 sub = argparse.Namespace(**vars(args))
                 sub.workload, sub.copies = name, None
                 if batch is not None:
                     sub.batch = batch
-                    if shared is None:
-                        shared = _decode_weights(local_rank, rank)
+                    if shared is None:  # sharded steps need the same weights on every rank
+                        shared = _decode_weights(local_rank, rank if name == "gemma-decode" else 0)
                 rec = _run_one(sub, rank, world, local_rank, shared)
                 if rec is not None:
                     subs[name if batch is None else f"{name}-b{batch}"] = rec

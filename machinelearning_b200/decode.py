@@ -102,6 +102,20 @@ def padded_k(k: int, batch: int) -> int:
     return (k // 256 + 1) * 256
 
 
+def _rows(data, n: int, row_bytes: int, r0: int, r1: int):
+    """Rows [r0, r1) of an [n][row_bytes] byte matrix (numpy or CUDA tensor)."""
+    if isinstance(data, torch.Tensor):
+        return data.view(n, row_bytes)[r0:r1].contiguous().view(-1)
+    return np.ascontiguousarray(np.asarray(data, dtype=np.uint8).reshape(n, row_bytes)[r0:r1]).ravel()
+
+
+def _cols(data, n: int, row_bytes: int, c0: int, c1: int):
+    """Bytes [c0, c1) of every row of an [n][row_bytes] byte matrix."""
+    if isinstance(data, torch.Tensor):
+        return data.view(n, row_bytes)[:, c0:c1].contiguous().view(-1)
+    return np.ascontiguousarray(np.asarray(data, dtype=np.uint8).reshape(n, row_bytes)[:, c0:c1]).ravel()
+
+
 def band_k(k: int) -> int:
     """Columns the lm_head is padded to at batch 1: a 16-byte row pitch lets its
     one-token matmul stream through the band GEMV."""
@@ -111,10 +125,24 @@ def band_k(k: int) -> int:
 class Gemma3Decoder:
     """Weights: the dict layout of the parity oracle (``emb`` Q8_0 bytes,
     ``final_norm``, per layer ``qkv``/``o``/``gate``/``up``/``down`` Q4_0 bytes
-    and the six norm vectors), as host numpy arrays or CUDA uint8 tensors."""
+    and the six norm vectors), as host numpy arrays or CUDA uint8 tensors.
 
-    def __init__(self, cfg: Gemma3Config, weights: dict, batch: int, device: int = 0, fused_attention: bool = True):
+    ``comm`` (a ``tp.TpComm`` of W > 1 ranks, one decoder per rank) shards the
+    step tensor-parallel: the feed-forward block Megatron-style (gate/up rows
+    [r F/W, (r+1) F/W) fused on each rank, down over the same K slice, one
+    all-reduce) and the tied lm_head by vocabulary rows (one all-gather of the
+    logits). Attention (4 query heads, 1 KV head) and the norms are replicated
+    on every rank. The sharded step runs its launches directly (the library's
+    non-blocking communicator is not captured in a CUDA graph)."""
+
+    def __init__(self, cfg: Gemma3Config, weights: dict, batch: int, device: int = 0, fused_attention: bool = True,
+                 comm=None):
         self.cfg, self.batch, self.device = cfg, batch, device
+        self.comm = comm if comm is not None and comm.world > 1 else None
+        W, R = (self.comm.world, self.comm.rank) if self.comm else (1, 0)
+        if cfg.ffn % (32 * W) or cfg.vocab % W:
+            raise ValueError(f"ffn {cfg.ffn} / vocab {cfg.vocab} do not shard over {W} ranks")
+        self.ffn_local, self.vocab_local = cfg.ffn // W, cfg.vocab // W
         self.fused_attention = fused_attention  # QK-norm/RoPE/cache append inside the attention kernel
         dev = torch.device("cuda", device)
         self.dev = dev
@@ -130,18 +158,25 @@ class Gemma3Decoder:
         # the lm_head also at batch 1: a 16-byte row pitch lets its one-token
         # matmul stream through the band kernel
         self.klm = klm = kh if batch != 1 else band_k(H)
-        self.lm_head = self.emb if klm == H else _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device, klm)
+        Fl, Vl = self.ffn_local, self.vocab_local
+        if self.comm:  # this rank's vocabulary rows
+            lm = _rows(weights["emb"], cfg.vocab, (H // 32) * 34, R * Vl, (R + 1) * Vl)
+            self.lm_head = _quant_weight(Q8_0, Vl, H, lm, device, klm)
+        else:
+            self.lm_head = self.emb if klm == H else _quant_weight(Q8_0, cfg.vocab, H, weights["emb"], device, klm)
         self.final_norm = vec(weights["final_norm"])
         self.layers = []
         nqkv = (nq + 2 * nkv) * hd
+        rb_h, rb_f = (H // 32) * 18, (cfg.ffn // 32) * 18
         for lw in weights["layers"]:
-            gate = _quant_weight(Q4_0, cfg.ffn, H, lw["gate"], device, kh)
-            up = _quant_weight(Q4_0, cfg.ffn, H, lw["up"], device, kh)
+            gate = _quant_weight(Q4_0, Fl, H, _rows(lw["gate"], cfg.ffn, rb_h, R * Fl, (R + 1) * Fl), device, kh)
+            up = _quant_weight(Q4_0, Fl, H, _rows(lw["up"], cfg.ffn, rb_h, R * Fl, (R + 1) * Fl), device, kh)
+            down = lw["down"] if W == 1 else _cols(lw["down"], H, rb_f, R * (Fl // 32) * 18, (R + 1) * (Fl // 32) * 18)
             layer = {
                 "qkv": _quant_weight(Q4_0, nqkv, H, lw["qkv"], device, kh),
                 "o": _quant_weight(Q4_0, H, nq * hd, lw["o"], device),
                 "gate_up": fuse_gate_up(gate, up),
-                "down": _quant_weight(Q4_0, H, cfg.ffn, lw["down"], device),
+                "down": _quant_weight(Q4_0, H, Fl, down, device),
             }
             gate.close()
             up.close()
@@ -160,15 +195,15 @@ class Gemma3Decoder:
         self.hp = self.h if kh == H else z(B, kh)  # h with a zero tail to kh columns
         self.hl = self.hp if klm == kh else z(B, klm)  # the same for the lm_head
         self.qkv, self.q, self.attn = z(B, nqkv), z(B, nq * hd), z(B, nq * hd)
-        self.ff = z(B, cfg.ffn)
+        self.ff = z(B, Fl)
         self.logits = z(B, cfg.vocab)
         self.part = z(int(self.lib.qmm_attention_partial_floats(B, nq, hd, cfg.ctx)))
         self.inv_scale = float(np.float32(1.0) / np.float32(math.sqrt(cfg.query_pre_attn_scalar)))
         self.stream = torch.cuda.Stream(dev)
         self.graph = None
         need = max(self.lib.qmm_workspace_size(dt, 0, B, n, k) for dt, n, k in
-                   [(Q4_0, nqkv, kh), (Q4_0, H, nq * hd), (Q4_0, 2 * cfg.ffn, kh), (Q4_0, H, cfg.ffn),
-                    (Q8_0, cfg.vocab, klm)])
+                   [(Q4_0, nqkv, kh), (Q4_0, H, nq * hd), (Q4_0, 2 * Fl, kh), (Q4_0, H, Fl),
+                    (Q8_0, Vl, klm)])
         _lib.check(self.lib.qmm_reserve_workspace(device, ctypes.c_void_p(self.stream.cuda_stream), need + (1 << 20)))
 
     # ---- one step, issued on self.stream ---------------------------------------------
@@ -201,14 +236,20 @@ class Gemma3Decoder:
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_attn_norm"]), P(lw["ffn_norm"]),
                                           cfg.offset, cfg.eps, B, H, P(self.hp), self.kh, sp))
             ck(L.qmm_gated_forward(lw["gate_up"].handle, P(self.hp), B, P(self.ff), GELU, sp))
-            ck(L.qmm_linear_forward(lw["down"].handle, P(self.ff), B, P(self.o), 0, sp))
+            if self.comm:  # this rank's K slice of down, summed over the ranks
+                ck(L.qmm_tp_row_forward(self.comm.handle, lw["down"].handle, P(self.ff), B, P(self.o), 0, sp))
+            else:
+                ck(L.qmm_linear_forward(lw["down"].handle, P(self.ff), B, P(self.o), 0, sp))
             nxt = self.layers[li + 1]["attn_norm"] if li + 1 < len(self.layers) else self.final_norm
             ck(L.qmm_residual_rmsnorm_dev(P(self.x), P(self.o), P(lw["post_ffn_norm"]), P(nxt), cfg.offset, cfg.eps,
                                           B, H, P(self.hp), self.kh, sp))
         if self.hl is not self.hp:  # batch 1: only the lm_head reads a padded copy
             with torch.cuda.stream(self.stream):
                 self.hl[:, :H].copy_(self.hp)
-        ck(L.qmm_linear_forward(self.lm_head.handle, P(self.hl), B, P(self.logits), 0, sp))
+        if self.comm:  # this rank's vocabulary rows, gathered into [B][vocab]
+            ck(L.qmm_tp_column_forward(self.comm.handle, self.lm_head.handle, P(self.hl), B, P(self.logits), 0, sp))
+        else:
+            ck(L.qmm_linear_forward(self.lm_head.handle, P(self.hl), B, P(self.logits), 0, sp))
         if advance:
             ck(L.qmm_add_int_dev(P(self.pos), 1, sp))
 
@@ -228,7 +269,11 @@ class Gemma3Decoder:
 
     def capture(self, advance: bool = True) -> None:
         """Record one step (and, with ``advance``, the position increment) as a
-        CUDA graph; later ``step()`` calls replay it."""
+        CUDA graph; later ``step()`` calls replay it. A sharded decoder keeps
+        launching directly (its communicator is not captured)."""
+        if self.comm:
+            self.graph = None
+            return
         # one direct launch first (it rewrites this position's cache rows with
         # the same values): kernel attributes are set outside the capture
         with torch.cuda.stream(self.stream):
@@ -254,6 +299,15 @@ class Gemma3Decoder:
         # work queued on the caller's stream after this call sees the logits
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)
         return self.logits
+
+    def wait(self, timeout_s: float = 60.0) -> None:
+        """Waits for the step's work; a sharded decoder through its
+        communicator (a stuck or failed collective raises QmmError with
+        QMM_ERR_TIMEOUT / QMM_ERR_NCCL instead of hanging)."""
+        if self.comm:
+            _lib.check(self.comm.wait(timeout_s, self.stream))
+        else:
+            self.stream.synchronize()
 
     def close(self) -> None:
         self.graph = None

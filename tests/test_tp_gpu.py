@@ -7,7 +7,8 @@ an init whose peer never joins returns QMM_ERR_TIMEOUT (host bootstrap only:
 no kernel runs).
 
 Two GPUs (skipped with fewer): the column-parallel, row-parallel and
-Megatron-paired feed-forward against the oracle's single-process result
+Megatron-paired feed-forward and the sharded Gemma-3 decode step against the
+oracle's single-process result
 (column-parallel Q8_0-activation outputs bit-exact; f32 outputs and sums within
 the 1e-3 contract), then a rank that leaves between steps: the other learns it
 on the host (StepGuard) before launching its next collective and returns
@@ -157,6 +158,27 @@ def _worker(rank: int, world: int, port: int):
     u = oracle.matmul_f32_q4(x.ravel(), uw, m, dim, hidden).reshape(m, hidden)
     h = (oracle.gelu(g.ravel()).reshape(m, hidden) * u).astype(np.float32)
     assert_close_rel(y.cpu().numpy().ravel(), oracle.matmul_f32_q4(h.ravel(), dw, m, hidden, dim), 1e-3)
+    # the sharded Gemma-3 decode step (FFN Megatron-paired, lm_head by
+    # vocabulary rows) against the oracle's pass, batch 1 and 3, 3 positions
+    from oracle.decode import decode_step
+    from test_decode_gpu import host_weights, small_config
+
+    from machinelearning_b200.decode import Gemma3Decoder
+    cfg = small_config(256)
+    hw = host_weights(oracle, cfg, seed=21)
+    for B in (1, 3):
+        dec = Gemma3Decoder(cfg, hw, batch=B, device=rank, comm=comm)
+        kc = [np.zeros((B, cfg.n_kv_heads, cfg.ctx, cfg.head_dim), np.float32) for _ in range(cfg.n_layers)]
+        vc = [np.zeros_like(kc[0]) for _ in range(cfg.n_layers)]
+        rng = np.random.default_rng(31 + B)  # the same token ids on both ranks
+        dec.set_position(0)
+        for pos in range(3):
+            tokens = rng.integers(0, cfg.vocab, B)
+            got = dec.step(tokens)
+            dec.wait(60.0)
+            ref = decode_step(cfg, hw, tokens, pos, kc, vc)
+            assert_close_rel(got.cpu().numpy().ravel(), ref.ravel(), 1e-3)
+        dec.close()
     # rank 1 leaves between steps; rank 0 learns it on the host, launches nothing
     guard = StepGuard(default_store(), rank, world, timeout_s=3.0, prefix="tp_gpu_leave")
     buf = torch.ones(1024, device="cuda")

@@ -215,7 +215,6 @@ __global__ void __launch_bounds__(kDecThreads) qk_rope_cache_kernel(
 // head. q heads of one kv head share its rows.
 constexpr int kAttnChunk = 32;
 constexpr int kMaxHeads = 8;
-constexpr int kMaxHd = 256;
 __host__ __device__ constexpr size_t attn_smem_bytes(int hd) {
     return (size_t)(kAttnChunk * (hd + 1) + kAttnChunk * hd + kMaxHeads * hd + kMaxHeads * kAttnChunk) * 4;
 }

@@ -65,7 +65,6 @@ constexpr int kStepsPerChunk = 4;  // a raw chunk is 8 blocks = 256 elements
 __host__ __device__ constexpr int dq_warps(int W) { return W / 16; }
 __host__ __device__ constexpr int dq_threads(int W) { return 2 * W; }
 __host__ __device__ constexpr int gemm_threads(int W) { return 64 + dq_threads(W) + 32; }
-constexpr uint32_t kTileBytes = BM * BK * 2;  // 16 KB: 128 rows x 128 bytes (x16 tile)
 
 // Operand rings: the x16 (A) ring is the deeper one -- its TMA loads take
 // 1.5-2 us to land under load, and a stage is refilled only once the MMAs

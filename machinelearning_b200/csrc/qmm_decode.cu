@@ -208,22 +208,86 @@ __global__ void __launch_bounds__(kDecThreads) qk_rope_cache_kernel(
 
 // Partial attention over positions [c*kAttnChunk, ...] <= pos of one token b.
 // The chunk's K and V rows are staged in shared memory with 16-byte loads
-// (all in flight together; K rows padded by one float so that threads reading
-// different rows at one column hit different banks), then: thread (h, t)
-// computes one score q_h . k_t * inv_scale; per head m = max, e_t = exp(s_t -
-// m), l = sum e_t; thread d accumulates acc_h[d] = sum_t e_t v_t[d] for every
-// head. q heads of one kv head share its rows.
+// (all in flight together), then: thread (h, t) computes one score q_h . k_t *
+// inv_scale in 16-byte steps; per head m = max, e_t = exp(s_t - m), l = sum
+// e_t; thread (h, 4 columns) accumulates acc_h[d] = sum_t e_t v_t[d] in 16-byte
+// steps. q heads of one kv head share its rows. K row t is stored rotated by t
+// 16-byte units (unit u at (u + t) mod hd/4), so the 32 threads of a warp,
+// each reading its own row at the same logical unit, hit distinct banks.
 constexpr int kAttnChunk = 32;
 constexpr int kMaxHeads = 8;
 __host__ __device__ constexpr size_t attn_smem_bytes(int hd) {
-    return (size_t)(kAttnChunk * (hd + 1) + kAttnChunk * hd + kMaxHeads * hd + kMaxHeads * kAttnChunk) * 4;
+    return (size_t)(2 * kAttnChunk * hd + kMaxHeads * hd + kMaxHeads * kAttnChunk) * 4;
+}
+// Shared float index of element d of K row t in the rotated layout.
+__device__ __forceinline__ int krot(int t, int d, int hd4) {
+    int u = (d >> 2) + t % hd4;
+    if (u >= hd4) u -= hd4;
+    return (t * hd4 + u) * 4 + (d & 3);
+}
+// Scores, softmax and weighted V of kv head kv's q heads over the chunk's len
+// staged positions; the partial (acc[hd], m, l) of each head to pbase.
+__device__ __forceinline__ void attn_chunk(const float* qs, const float* ks, const float* vs, float* sc, int kv,
+                                           int g, int len, int hd, float inv_scale, float* pbase) {
+    const int hd4 = hd / 4;
+    for (int i = threadIdx.x; i < g * len; i += blockDim.x) {
+        const int hh = i / len, t = i - hh * len;
+        const float4* q4 = reinterpret_cast<const float4*>(qs + (kv * g + hh) * hd);
+        const float4* k4 = reinterpret_cast<const float4*>(ks) + t * hd4;
+        const int rot = t % hd4;
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        for (int u = 0; u < hd4; ++u) {
+            int pu = u + rot;
+            if (pu >= hd4) pu -= hd4;
+            const float4 a = q4[u], b = k4[pu];
+            s0 = fmaf(a.x, b.x, s0);
+            s1 = fmaf(a.y, b.y, s1);
+            s2 = fmaf(a.z, b.z, s2);
+            s3 = fmaf(a.w, b.w, s3);
+        }
+        sc[(kv * g + hh) * kAttnChunk + t] = ((s0 + s1) + (s2 + s3)) * inv_scale;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < g) {  // per head: max, exponentials, their sum
+        const int h = kv * g + threadIdx.x;
+        float* e = sc + h * kAttnChunk;
+        float m = -INFINITY;
+        for (int t = 0; t < len; ++t) m = fmaxf(m, e[t]);
+        float l = 0.0f;
+        for (int t = 0; t < len; ++t) {
+            e[t] = expf(e[t] - m);
+            l += e[t];
+        }
+        pbase[h * (hd + 2) + hd] = m;
+        pbase[h * (hd + 2) + hd + 1] = l;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < g * hd4; i += blockDim.x) {
+        const int hh = i / hd4, u = i - hh * hd4;
+        const float* e = sc + (kv * g + hh) * kAttnChunk;
+        const float4* v4 = reinterpret_cast<const float4*>(vs) + u;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int t = 0; t < len; ++t) {
+            const float w = e[t];
+            const float4 v = v4[t * hd4];
+            acc.x = fmaf(w, v.x, acc.x);
+            acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z);
+            acc.w = fmaf(w, v.w, acc.w);
+        }
+        float* o = pbase + (kv * g + hh) * (hd + 2) + 4 * u;
+        o[0] = acc.x;
+        o[1] = acc.y;
+        o[2] = acc.z;
+        o[3] = acc.w;
+    }
 }
 __global__ void __launch_bounds__(kDecThreads) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache, int nq,
     int nkv, int hd, const int* __restrict__ pos_dev, int ctx, float inv_scale, float* __restrict__ part) {
     extern __shared__ float asm_[];
-    float* ks = asm_;                           // [kAttnChunk][hd + 1]
-    float* vs = ks + kAttnChunk * (hd + 1);     // [kAttnChunk][hd]
+    float* ks = asm_;                           // [kAttnChunk][hd], rows rotated (krot)
+    float* vs = ks + kAttnChunk * hd;           // [kAttnChunk][hd]
     float* qs = vs + kAttnChunk * hd;           // [nq][hd]
     float* sc = qs + kMaxHeads * hd;            // [nq][kAttnChunk]
     const int c = blockIdx.x, b = blockIdx.y;
@@ -250,53 +314,22 @@ __global__ void __launch_bounds__(kDecThreads) attn_partial_kernel(
         for (int i = threadIdx.x; i < len * hd4; i += blockDim.x) {
             const int t = i / hd4, j = i - t * hd4;
             const float4 kv4 = kc[i], vv4 = vc[i];
-            float* kr = ks + t * (hd + 1) + 4 * j;
-            kr[0] = kv4.x;
-            kr[1] = kv4.y;
-            kr[2] = kv4.z;
-            kr[3] = kv4.w;
+            *reinterpret_cast<float4*>(ks + krot(t, 4 * j, hd4)) = kv4;
             reinterpret_cast<float4*>(vs)[i] = vv4;
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < g * len; i += blockDim.x) {
-            const int hh = i / len, t = i - hh * len;
-            const float* qh = qs + (kv * g + hh) * hd;
-            const float* kr = ks + t * (hd + 1);
-            float sacc = 0.0f;
-            for (int d = 0; d < hd; ++d) sacc += qh[d] * kr[d];
-            sc[(kv * g + hh) * kAttnChunk + t] = sacc * inv_scale;
-        }
-        __syncthreads();
-        if ((int)threadIdx.x < g) {  // per head: max, exponentials, their sum
-            const int h = kv * g + threadIdx.x;
-            float* e = sc + h * kAttnChunk;
-            float m = -INFINITY;
-            for (int t = 0; t < len; ++t) m = fmaxf(m, e[t]);
-            float l = 0.0f;
-            for (int t = 0; t < len; ++t) {
-                e[t] = expf(e[t] - m);
-                l += e[t];
-            }
-            pbase[h * (hd + 2) + hd] = m;
-            pbase[h * (hd + 2) + hd + 1] = l;
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < g * hd; i += blockDim.x) {
-            const int hh = i / hd, d = i - hh * hd;
-            const float* e = sc + (kv * g + hh) * kAttnChunk;
-            float acc = 0.0f;
-            for (int t = 0; t < len; ++t) acc += e[t] * vs[t * hd + d];
-            pbase[(kv * g + hh) * (hd + 2) + d] = acc;
-        }
+        attn_chunk(qs, ks, vs, sc, kv, g, len, hd, inv_scale, pbase);
     }
 }
 
 // One head vector (hd values, one warp): rot -- RMSNorm with weight nw and
 // half-split RoPE with the position's cos/sin rows; else a copy. Written to
-// dst_a and, if non-null, dst_b (both contiguous over the vector).
+// dst_a (contiguous) and, if non-null, dst_b: contiguous, or, with b_row >= 0,
+// as row b_row of a rotated K stage (krot).
 __device__ __forceinline__ void norm_rope_vec(const float* __restrict__ src, const float* __restrict__ nw, bool rot,
                                               float offset, float eps, int hd, const float* __restrict__ ct,
-                                              const float* __restrict__ st, int lane, float* dst_a, float* dst_b) {
+                                              const float* __restrict__ st, int lane, float* dst_a, float* dst_b,
+                                              int b_row = -1) {
     const int half = hd / 2, per = half / 32;
     float x1[4], x2[4];
 #pragma unroll
@@ -328,7 +361,10 @@ __device__ __forceinline__ void norm_rope_vec(const float* __restrict__ src, con
             }
             dst_a[i] = r1;
             dst_a[half + i] = r2;
-            if (dst_b) {
+            if (dst_b && b_row >= 0) {
+                dst_b[krot(b_row, i, hd / 4)] = r1;
+                dst_b[krot(b_row, half + i, hd / 4)] = r2;
+            } else if (dst_b) {
                 dst_b[i] = r1;
                 dst_b[half + i] = r2;
             }
@@ -347,8 +383,8 @@ __global__ void __launch_bounds__(kDecThreads) attn_fused_kernel(
     const float* __restrict__ sin_t, const int* __restrict__ pos_dev, int ctx, float* __restrict__ k_cache,
     float* __restrict__ v_cache, float inv_scale, float* __restrict__ part) {
     extern __shared__ float asm_[];
-    float* ks = asm_;                           // [kAttnChunk][hd + 1]
-    float* vs = ks + kAttnChunk * (hd + 1);     // [kAttnChunk][hd]
+    float* ks = asm_;                           // [kAttnChunk][hd], rows rotated (krot)
+    float* vs = ks + kAttnChunk * hd;           // [kAttnChunk][hd]
     float* qs = vs + kAttnChunk * hd;           // [nq][hd]
     float* sc = qs + kMaxHeads * hd;            // [nq][kAttnChunk]
     const int c = blockIdx.x, b = blockIdx.y;
@@ -385,7 +421,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_fused_kernel(
                 norm_rope_vec(src + (size_t)h * hd, qn_w, true, offset, eps, hd, ct, st, lane, qs + h * hd, nullptr);
             } else if (v == g) {
                 norm_rope_vec(src + (size_t)(nq + kv) * hd, kn_w, true, offset, eps, hd, ct, st, lane,
-                              k_cache + (((size_t)b * nkv + kv) * ctx + pos) * hd, ks + tp * (hd + 1));
+                              k_cache + (((size_t)b * nkv + kv) * ctx + pos) * hd, ks, tp);
             } else {
                 norm_rope_vec(src + (size_t)(nq + nkv + kv) * hd, nullptr, false, offset, eps, hd, ct, st, lane,
                               v_cache + (((size_t)b * nkv + kv) * ctx + pos) * hd, vs + tp * hd);
@@ -394,45 +430,11 @@ __global__ void __launch_bounds__(kDecThreads) attn_fused_kernel(
         for (int i = threadIdx.x; i < len * hd4; i += blockDim.x) {
             const int t = i / hd4, j = i - t * hd4;
             if (owner && t == tp) continue;  // written above
-            const float4 kv4 = kc[i], vv4 = vc[i];
-            float* kr = ks + t * (hd + 1) + 4 * j;
-            kr[0] = kv4.x;
-            kr[1] = kv4.y;
-            kr[2] = kv4.z;
-            kr[3] = kv4.w;
-            reinterpret_cast<float4*>(vs)[i] = vv4;
+            *reinterpret_cast<float4*>(ks + krot(t, 4 * j, hd4)) = kc[i];
+            reinterpret_cast<float4*>(vs)[i] = vc[i];
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < g * len; i += blockDim.x) {
-            const int hh = i / len, t = i - hh * len;
-            const float* qh = qs + (kv * g + hh) * hd;
-            const float* kr = ks + t * (hd + 1);
-            float sacc = 0.0f;
-            for (int d = 0; d < hd; ++d) sacc += qh[d] * kr[d];
-            sc[(kv * g + hh) * kAttnChunk + t] = sacc * inv_scale;
-        }
-        __syncthreads();
-        if ((int)threadIdx.x < g) {  // per head: max, exponentials, their sum
-            const int h = kv * g + threadIdx.x;
-            float* e = sc + h * kAttnChunk;
-            float m = -INFINITY;
-            for (int t = 0; t < len; ++t) m = fmaxf(m, e[t]);
-            float l = 0.0f;
-            for (int t = 0; t < len; ++t) {
-                e[t] = expf(e[t] - m);
-                l += e[t];
-            }
-            pbase[h * (hd + 2) + hd] = m;
-            pbase[h * (hd + 2) + hd + 1] = l;
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < g * hd; i += blockDim.x) {
-            const int hh = i / hd, d = i - hh * hd;
-            const float* e = sc + (kv * g + hh) * kAttnChunk;
-            float acc = 0.0f;
-            for (int t = 0; t < len; ++t) acc += e[t] * vs[t * hd + d];
-            pbase[(kv * g + hh) * (hd + 2) + d] = acc;
-        }
+        attn_chunk(qs, ks, vs, sc, kv, g, len, hd, inv_scale, pbase);
     }
 }
 

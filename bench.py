@@ -320,6 +320,12 @@ def run_ours(args, rank, world, local_rank):
         else:
             assert (k // 32) % world == 0, f"{name}: K={k} blocks not divisible by {world}"
             problems.append((name, k // world, n, dt, kind, k, n))
+    if comm is not None and args.join == "peer":
+        # joins over peer memory: buffers for the largest joined output
+        # (column: [batch][N]; row: every rank's [batch][N] partial)
+        cap = max(4 * b * (n if kind in ("col", "gated") else world * n)
+                  for b in wl["batches"] for (_, kl, n_l, dt, kind, k, n) in problems)
+        comm.enable_peer(cap)
 
     gen = torch.Generator(device=dev)
 
@@ -500,8 +506,11 @@ def run_ours(args, rank, world, local_rank):
                 "projections": [f"{p[0]} {p[5]}->{p[6]}{' x2 (fused, SwiGLU epilogue)' if p[4] == 'gated' else ''} "
                                 f"{'Q8_0' if p[3] == Q8_0 else 'Q4_0'} {p[4]}" for p in problems],
                 "batches": wl["batches"],
-                "parallelism": (f"tp{world} (libqmm NCCL communicator: column-parallel all-gather, row-parallel "
-                                f"all-reduce)" if world > 1 else "single"),
+                "parallelism": ((f"tp{world} (libqmm communicator; joins over peer memory: GEMV / GEMM epilogues "
+                                 f"store into every rank's buffer over NVLink, one flag-barrier kernel per join)"
+                                 if args.join == "peer" else
+                                 f"tp{world} (libqmm NCCL communicator: column-parallel all-gather, row-parallel "
+                                 f"all-reduce)") if world > 1 else "single"),
                 "l2": f"{copies} weight copies rotated" + (" (>L2)" if copies > 1 else "; weights > L2"),
                 "algorithmic_bytes_per_step": steps_bytes,
                 "algorithmic_flops_per_step": sum(2 * gemvs_of(kind) * b * k * n for b in wl["batches"]
@@ -798,6 +807,8 @@ def run_decode(args, rank, world, local_rank, shared=None):
     # a sharded step needs the same weights on every rank
     cfg, w = shared if shared is not None else _decode_weights(local_rank, 0 if tp else rank)
     comm = TpComm.from_group(local_rank, timeout_s=120.0) if tp else None
+    if comm is not None and args.join == "peer":
+        comm.enable_peer(4 * args.batch * max(cfg.vocab, world * cfg.hidden))
     model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank, comm=comm)
     L = _lib.lib()
     dev = model.dev
@@ -889,7 +900,8 @@ def run_decode(args, rank, world, local_rank, shared=None):
                        "model": WORKLOADS["gemma-decode"]["model"],
                        "batch": B, "position": DECODE_POS, "kv_context": cfg.ctx,
                        "parallelism": (f"tp{world}: FFN Megatron-paired, lm_head vocabulary-parallel, attention "
-                                       f"replicated (libqmm NCCL communicator)" if tp else
+                                       f"replicated (libqmm communicator, "
+                                       f"{'joins over peer memory' if args.join == 'peer' else 'NCCL joins'})" if tp else
                                        (f"{world} replicas" if world > 1 else "single")),
                        "graph": ("direct launches (sharded step: the non-blocking communicator is not captured)"
                                  if tp else "one CUDA graph per step (embedding, 26 layers, final norm, lm_head)"),
@@ -1009,6 +1021,8 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
     ap.add_argument("--no-sub", action="store_true", help="default run without the other configurations' records")
     ap.add_argument("--batch", type=int, default=1, help="gemma-decode: sequences per step (1, 16, 64)")
+    ap.add_argument("--join", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: join tensor-parallel outputs over peer memory (default) or with NCCL collectives")
     ap.add_argument("--copies", type=int, default=None,
                     help="weight copies rotated (default: the workload's; fewer for short profiling runs)")
     args = ap.parse_args(argv)

@@ -67,6 +67,25 @@ QMM_API int qmm_tp_abort(qmm_tp_comm* comm);
 
 QMM_API int qmm_tp_rank(const qmm_tp_comm* comm, int* rank, int* world);
 
+/* Joins over peer memory instead of NCCL collectives (collective; every rank
+ * calls it once, after qmm_tp_init). Each rank allocates a flag array and two
+ * join buffers of `bytes` each and maps every other rank's through CUDA IPC
+ * (NVLink peer access; the handles travel through the communicator). From
+ * then on, qmm_tp_column_forward / qmm_tp_row_forward whose joined result fits
+ * in `bytes` write it straight into every rank's buffer -- from the producing
+ * kernel's own epilogue where that kernel supports it (the band GEMV and the
+ * f16 tensor-core GEMM), else by a copy kernel -- and one join kernel per call
+ * stores this rank's epoch into every peer's flags (release, system scope),
+ * waits for every peer's (acquire; bounded by the communicator's time limit)
+ * and reads the buffer out into y: a copy (column), or the sum over ranks in
+ * rank order (row; every rank then holds identical bits). Calls that do not
+ * fit, or that run under stream capture, join through NCCL as before. A
+ * join waits at most `join_timeout_s` seconds for a peer's signal (<= 0: the
+ * communicator's time limit); one whose wait runs out records it on the
+ * device, and the next qmm_tp_wait returns QMM_ERR_TIMEOUT and aborts the
+ * communicator. At most 8 ranks. */
+QMM_API int qmm_tp_enable_peer(qmm_tp_comm* comm, size_t bytes, double join_timeout_s);
+
 /* One poll of ncclCommGetAsyncError: QMM_OK, or (after an abort)
  * QMM_ERR_NCCL with the NCCL error string in qmm_last_error_message(). */
 QMM_API int qmm_tp_status(qmm_tp_comm* comm);

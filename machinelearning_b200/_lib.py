@@ -104,6 +104,7 @@ SIGNATURES = {
     "qmm_tp_destroy": (_I, [_P]),
     "qmm_tp_abort": (_I, [_P]),
     "qmm_tp_rank": (_I, [_P, _P, _P]),
+    "qmm_tp_enable_peer": (_I, [_P, _SZ, ctypes.c_double]),
     "qmm_tp_status": (_I, [_P]),
     "qmm_tp_wait": (_I, [_P, _P, ctypes.c_double]),
     "qmm_tp_column_forward": (_I, [_P, _P, _P, _SZ, _P, _I, _P]),

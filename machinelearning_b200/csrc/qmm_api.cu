@@ -189,6 +189,20 @@ int run_matmul(int dt, int act, const float* x, const uint8_t* w, size_t m, size
         if (e != cudaSuccess) return cuda_fail(e, "launch_gemm");
         return QMM_OK;
     }
+    // a join written by the kernel itself addresses whole [M][N] outputs: not
+    // offered to a GEMV that runs in row chunks
+    struct HidePeer {
+        PeerOut* saved = nullptr;
+        explicit HidePeer(bool hide) {
+            if (hide) {
+                saved = peer_out();
+                set_peer_out(nullptr);
+            }
+        }
+        ~HidePeer() {
+            if (saved) set_peer_out(saved);
+        }
+    } hide(m > kMaxGemvRows);
     for (size_t r0 = 0; r0 < m; r0 += kMaxGemvRows) {
         const size_t rows = (m - r0) < kMaxGemvRows ? (m - r0) : kMaxGemvRows;
         GemvPlan p;
@@ -222,6 +236,21 @@ int* device_error_word(int device) {
     }
     cache[device] = static_cast<int*>(p);
     return static_cast<int*>(p);
+}
+
+namespace {
+thread_local PeerOut* t_peer_out = nullptr;
+}
+PeerOut* peer_out() { return t_peer_out; }
+void set_peer_out(PeerOut* p) { t_peer_out = p; }
+void take_peer_out(PeerDst& out, bool supported) {
+    out.n = 0;
+    PeerOut* p = t_peer_out;
+    if (!p || !supported || p->taken || p->n < 1 || p->n > kMaxPeers) return;
+    for (int r = 0; r < kMaxPeers; ++r) out.dst[r] = r < p->n ? p->dst[r] : nullptr;
+    out.n = p->n;
+    out.ld = p->ld;
+    p->taken = true;
 }
 }  // namespace qmm
 

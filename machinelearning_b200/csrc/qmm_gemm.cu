@@ -106,6 +106,7 @@ struct GArgs {
     int gact;        // >= 0: gate/up epilogue (GatedOut), y unused
     float* gout;     // [M][ghidden]
     int64_t ghidden;
+    PeerDst peer;    // n > 0: the outputs go to every rank's join buffer instead of y
 };
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -328,7 +329,9 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
     constexpr int PITCH = raw_pitch_p(QT, P);
     constexpr int SR = raw_stages(QT, T, W, H, P);
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned by pointer arithmetic on the shared array (an integer
+    // round trip would hide the shared address space: generic loads)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = smem;                        // [SA][T] x16 tiles
     uint8_t* sB = smem + SA * T * kATile;      // [SB] weight tiles
     uint8_t* sR = sB + SB * kBTile;            // [SR] raw chunks
@@ -650,6 +653,10 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
             }
         }
         const bool vec = ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) && (a.N % 4 == 0);
+        // tensor-parallel join: the tile goes to the same place in every
+        // rank's buffer (peer memory over NVLink) instead of y; the launcher
+        // offers it only for 16-byte aligned destinations and rows
+        const int nout = a.peer.n > 0 ? a.peer.n : 1;
         for (int c4 = lane; c4 < W / 4; c4 += 32)
         for (int r = warp - 2; r < T * BMk && store && a.gact < 0; r += kDqWarps) {
             const int n = n0 + 4 * c4;
@@ -657,14 +664,17 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
             if (m >= a.M) break;  // rows are in increasing order
             const float sc = a.xs[m];
             const float4 v = *reinterpret_cast<const float4*>(ys + r * YP + 4 * c4);
-            float* yr = a.y + (int64_t)m * a.N + n;
-            if (vec && n + 3 < a.N) {
-                *reinterpret_cast<float4*>(yr) = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
-            } else {
-                if (n < a.N) yr[0] = v.x * sc;
-                if (n + 1 < a.N) yr[1] = v.y * sc;
-                if (n + 2 < a.N) yr[2] = v.z * sc;
-                if (n + 3 < a.N) yr[3] = v.w * sc;
+            const float4 o = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
+            for (int q = 0; q < nout; ++q) {
+                float* yr = a.peer.n > 0 ? a.peer.dst[q] + (int64_t)m * a.peer.ld + n : a.y + (int64_t)m * a.N + n;
+                if ((vec || a.peer.n > 0) && n + 3 < a.N) {
+                    *reinterpret_cast<float4*>(yr) = o;
+                } else {
+                    if (n < a.N) yr[0] = o.x;
+                    if (n + 1 < a.N) yr[1] = o.y;
+                    if (n + 2 < a.N) yr[2] = o.z;
+                    if (n + 3 < a.N) yr[3] = o.w;
+                }
             }
         }
     }
@@ -885,6 +895,14 @@ cudaError_t launch_gemm(int qt, const uint8_t* w, const float* x, float* y, int 
     a.ghidden = g.hidden;
     a.nb = K / QK;
     a.row_bytes = row_bytes;
+    {
+        // a join written from the epilogue: float4 stores need 16-byte aligned
+        // destinations and rows
+        const PeerOut* po = peer_out();
+        bool ok = g.act < 0 && po && N % 4 == 0 && po->ld % 4 == 0;
+        for (int r = 0; ok && r < po->n; ++r) ok = (reinterpret_cast<uintptr_t>(po->dst[r]) & 15) == 0;
+        take_peer_out(a.peer, ok);
+    }
     const void* fn = gemm_kernel_for(qt, T, W, half, paired);
     const size_t smem = gemm_smem_bytes(qt, T, W, half, paired);
     e = ensure_dynamic_smem(fn, smem);

@@ -214,7 +214,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
     constexpr int YP = kI8Rows + 4;                      // staging pitch in floats
     static_assert(NT * YP * 4 <= kI8SA * AST, "staging tile must fit in the weight ring");
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned by pointer arithmetic on the shared array (an integer
+    // round trip would hide the shared address space: generic loads)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = smem;                  // [SA] weight stages
     uint8_t* sX = sA + kI8SA * AST;      // [SX] activation stages
     uint8_t* sR = sX + kI8SX * XST;      // [SR] raw chunks

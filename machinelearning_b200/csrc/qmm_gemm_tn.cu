@@ -345,7 +345,9 @@ __global__ void __launch_bounds__(kTnThreads, 1) gemm_tn_kernel(const __grid_con
     constexpr int G = NT / 4;           // tokens per lane quarter
     constexpr uint32_t kDCols = 256;    // accumulator columns (wh | wl)
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned by pointer arithmetic on the shared array (an integer
+    // round trip would hide the shared address space: generic loads)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sB = smem;                        // [SB] dequantised weight tiles
     uint8_t* sA = sB + kTnSB * kTnBTile;       // [SA] activation stack tiles
     uint8_t* sR = sA + SA * kATile;            // [SR] raw chunks

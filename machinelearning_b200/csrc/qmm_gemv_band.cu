@@ -52,6 +52,7 @@ struct BArgs {
     int gact;  // >= 0: gate/up epilogue (GatedOut), y unused
     float* gout;
     int64_t ghidden;
+    PeerDst peer;  // n > 0: the outputs go to every rank's join buffer instead of y
 };
 
 template <int W>
@@ -272,6 +273,17 @@ __global__ void __launch_bounds__(BandThreads<kBandWarps>::kTotal, 1)
                     if (m < a.M && row < kGateGroup && gi < a.ghidden)
                         a.gout[(int64_t)m * a.ghidden + gi] = gated_value(a.gact, v[m], up);
                 }
+            } else if (a.peer.n > 0) {
+                // tensor-parallel join: the same row of every rank's buffer
+                // (peer memory over NVLink), coalesced 128-byte warp stores
+#pragma unroll
+                for (int r = 0; r < kMaxPeers; ++r)
+                    if (r < a.peer.n) {
+                        float* d = a.peer.dst[r];
+#pragma unroll
+                        for (int m = 0; m < 8; ++m)
+                            if (m < a.M && n < a.N) d[(int64_t)m * a.peer.ld + n] = v[m];
+                    }
             } else {
 #pragma unroll
                 for (int m = 0; m < 8; ++m)
@@ -365,6 +377,7 @@ cudaError_t launch_gemv_band(const GemvPlan& p, const CUtensorMap& tmap, const f
     a.gact = g.act;
     a.gout = g.out;
     a.ghidden = g.hidden;
+    take_peer_out(a.peer, g.act < 0 && !no_host_alloc);
     void* args[] = {(void*)&a};
     return launch_pdl_kernel(fn, dim3(p.grid), dim3(band_threads()), p.smem, st, args);
 }

@@ -22,6 +22,32 @@ struct GatedOut {
     int64_t hidden = 0;
 };
 
+// Output of a tensor-parallel join written from the producing kernel's own
+// epilogue (qmm_tp.cu): while a request is set on the calling thread, a
+// launcher that supports it (the band GEMV and the f16 GEMM, plain outputs)
+// stores element (m, n) at dst[r] + m * ld + n for every rank r -- peer
+// memory over NVLink, this rank's own buffer among them -- instead of y, and
+// sets `taken`. Other kernels write y and leave it unset.
+constexpr int kMaxPeers = 8;
+struct PeerOut {
+    float* dst[kMaxPeers] = {};
+    int n = 0;
+    int64_t ld = 0;
+    bool taken = false;
+};
+PeerOut* peer_out();  // this thread's request (null: none)
+void set_peer_out(PeerOut* p);
+// Kernel-side copy of a request (plain data for __grid_constant__ arguments).
+struct PeerDst {
+    float* dst[kMaxPeers];
+    int n;
+    int64_t ld;
+};
+// Takes this thread's request when the launch can honour it (row-contiguous
+// [M][N] output, 16-byte aligned rows for vector stores): fills `out`, marks
+// the request taken. Otherwise `out.n` = 0.
+void take_peer_out(PeerDst& out, bool supported);
+
 // ---- quantisers / dequantiser (qmm_quant.cu) -----------------------------------
 cudaError_t launch_quantize_q8_0(const float* x, int64_t n, uint8_t* out, float* scales, bool rounded_inv,
                                  cudaStream_t st);

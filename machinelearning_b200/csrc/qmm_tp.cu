@@ -22,10 +22,12 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "../../include/qmm.h"
 #include "../../include/qmm_tp.h"
 #include "qmm_common.cuh"
+#include "qmm_kernels.cuh"
 
 namespace qmm {
 int set_last_error(int status, const std::string& msg);
@@ -137,6 +139,115 @@ __global__ void tp_reorder_kernel(const float* __restrict__ g, float* __restrict
     }
 }
 
+// ---- joins over peer memory (qmm_tp_enable_peer) ------------------------------------
+// Every rank owns one allocation, mapped into every other rank's address space
+// (CUDA IPC over NVLink): [flags: one u64 per rank][error word][buffer 0][buffer 1].
+// A join of epoch e writes rank s's part into buffer e % 2 of every rank --
+// from the producing kernel's epilogue (band GEMV, f16 GEMM) or, for other
+// kernels, tp_push_kernel -- then tp_join_kernel stores e into flags[s] of
+// every peer (release, system scope), waits until its own flags[r] >= e for
+// every peer r (acquire, bounded by a time limit), and reads its buffer out
+// into y (column: a copy; row: the sum over ranks in rank order, so every rank
+// holds the same bits). Two buffers suffice: a rank writes epoch e + 1 only
+// after it saw every peer's flag e, which each peer stores after it has read
+// out its epoch e - 1 buffer (stream order).
+constexpr size_t kFlagsOff = 0, kErrOff = 64, kBufOff = 256;
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Copies this rank's [rows][cols] result into every rank's buffer (row stride ld).
+struct PushArgs {
+    float* dst[qmm::kMaxPeers];
+    const float* src;
+    int64_t rows, cols, ld;
+    int n;
+};
+__global__ void tp_push_kernel(const __grid_constant__ PushArgs a) {
+    const int64_t total = a.rows * a.cols;
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = o / a.cols, j = o - i * a.cols;
+        const float v = a.src[o];
+#pragma unroll
+        for (int r = 0; r < qmm::kMaxPeers; ++r)
+            if (r < a.n) a.dst[r][i * a.ld + j] = v;
+    }
+}
+
+struct JoinArgs {
+    uint64_t* signal[qmm::kMaxPeers];  // &flags[rank] in rank r's allocation (null for this rank)
+    const uint64_t* flags;             // this rank's flags
+    int* errw;                         // this rank's error word
+    const float* buf;                  // this rank's buffer of the epoch
+    float* y;
+    int64_t count;  // elements of y (row join: also of each rank's slot)
+    uint64_t epoch;
+    long long limit_ns;
+    int world, rank, reduce, vec4;
+};
+__global__ void tp_join_kernel(const __grid_constant__ JoinArgs a) {
+    // everything this rank wrote for the epoch precedes this kernel in stream
+    // order; the release below publishes it to the peers
+    if (blockIdx.x == 0 && threadIdx.x < (unsigned)a.world && (int)threadIdx.x != a.rank) {
+        __threadfence_system();
+        st_release_sys(a.signal[threadIdx.x], a.epoch);
+    }
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        int good = 1;
+        const uint64_t t0 = global_ns();
+        for (int r = 0; r < a.world && good; ++r) {
+            if (r == a.rank) continue;
+            while (ld_acquire_sys(a.flags + r) < a.epoch) {
+                if ((long long)(global_ns() - t0) > a.limit_ns) {
+                    good = 0;
+                    atomicExch(a.errw, 1);
+                    break;
+                }
+                __nanosleep(128);
+            }
+        }
+        ok = good;
+    }
+    __syncthreads();
+    if (!ok) return;  // y is left as it was; the host reads the error word
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (a.vec4) {
+        const float4* b4 = reinterpret_cast<const float4*>(a.buf);
+        float4* y4 = reinterpret_cast<float4*>(a.y);
+        const int64_t n4 = a.count / 4;
+        for (int64_t i = t; i < n4; i += stride) {
+            float4 s = __ldcg(b4 + i);
+            for (int r = 1; a.reduce && r < a.world; ++r) {
+                const float4 v = __ldcg(b4 + r * n4 + i);
+                s.x += v.x;
+                s.y += v.y;
+                s.z += v.z;
+                s.w += v.w;
+            }
+            y4[i] = s;
+        }
+    } else {
+        for (int64_t i = t; i < a.count; i += stride) {
+            float s = __ldcg(a.buf + i);
+            for (int r = 1; a.reduce && r < a.world; ++r) s += __ldcg(a.buf + r * a.count + i);
+            a.y[i] = s;
+        }
+    }
+}
+
 }  // namespace
 
 struct qmm_tp_comm {
@@ -147,6 +258,14 @@ struct qmm_tp_comm {
     std::mutex mu;  // guards the gather buffer
     float* gbuf = nullptr;
     size_t gbytes = 0;
+    // joins over peer memory
+    uint8_t* xmem = nullptr;                   // this rank's allocation
+    uint8_t* pmem[qmm::kMaxPeers] = {};        // every rank's allocation as mapped here (own included)
+    size_t cap = 0;                            // bytes per buffer
+    uint64_t epoch = 0;
+    double join_timeout_s = 60.0;              // a join's wait for the peers' signals
+    bool peer_on = false;
+    bool peer_used = false;                    // a join ran since the last wait
 };
 
 namespace {
@@ -216,6 +335,102 @@ int gather_buffer(qmm_tp_comm* c, size_t bytes, cudaStream_t st, float** out) {
         c->gbytes = bytes;
     }
     *out = c->gbuf;
+    return QMM_OK;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+void release_peer(qmm_tp_comm* c) {
+    for (int r = 0; r < qmm::kMaxPeers; ++r) {
+        if (c->pmem[r] && r != c->rank) cudaIpcCloseMemHandle(c->pmem[r]);
+        c->pmem[r] = nullptr;
+    }
+    if (c->xmem) cudaFree(c->xmem);
+    c->xmem = nullptr;
+    c->peer_on = false;
+    cudaGetLastError();
+}
+
+// The join of one column- or row-parallel forward over peer memory. Returns
+// -1 when the join cannot take this call (not enabled, too large for the
+// buffers, or the stream is being captured: the epoch is a launch argument),
+// so the caller joins through NCCL instead.
+int peer_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t m, float* y, int act,
+                 cudaStream_t st, bool column, size_t cols) {
+    if (!c->peer_on) return -1;
+    const size_t W = (size_t)c->world;
+    const size_t count = column ? m * W * cols : m * cols;
+    const size_t need = (column ? count : W * count) * sizeof(float);
+    if (need > c->cap) return -1;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return -1;
+    }
+    const uint64_t e = c->epoch + 1;
+    const size_t par = (size_t)(e & 1) * c->cap;
+    float* own = reinterpret_cast<float*>(c->xmem + kBufOff + par);
+    qmm::PeerOut po;
+    po.n = c->world;
+    po.ld = column ? (int64_t)(W * cols) : (int64_t)cols;
+    const size_t part = column ? (size_t)c->rank * cols : (size_t)c->rank * m * cols;  // this rank's place
+    for (int r = 0; r < c->world; ++r) po.dst[r] = reinterpret_cast<float*>(c->pmem[r] + kBufOff + par) + part;
+    // where a kernel that cannot write the join itself leaves the result:
+    // contiguous [m][cols]
+    float* ylocal = own + part;
+    if (column && m > 1) {
+        int rc = gather_buffer(c, m * cols * sizeof(float), st, &ylocal);
+        if (rc) return rc;
+    }
+    qmm::set_peer_out(&po);
+    int rc = qmm_linear_forward(shard, x, m, ylocal, act, st);
+    qmm::set_peer_out(nullptr);
+    if (rc) return rc;
+    if (!po.taken) {
+        PushArgs pa;
+        for (int r = 0; r < qmm::kMaxPeers; ++r) pa.dst[r] = po.dst[r];
+        pa.src = ylocal;
+        pa.rows = (int64_t)m;
+        pa.cols = (int64_t)cols;
+        pa.ld = po.ld;
+        pa.n = c->world;
+        const int64_t total = pa.rows * pa.cols;
+        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 4);
+        qmm::note_launch();
+        tp_push_kernel<<<blocks, 256, 0, st>>>(pa);
+        const cudaError_t e1 = cudaGetLastError();
+        if (e1 != cudaSuccess) {
+            abort_comm(c);
+            return fail(QMM_ERR_CUDA, std::string("tp_push_kernel: ") + cudaGetErrorString(e1));
+        }
+    }
+    JoinArgs j;
+    for (int r = 0; r < qmm::kMaxPeers; ++r)
+        j.signal[r] = (r < c->world && r != c->rank)
+                          ? reinterpret_cast<uint64_t*>(c->pmem[r] + kFlagsOff) + c->rank
+                          : nullptr;
+    j.flags = reinterpret_cast<const uint64_t*>(c->xmem + kFlagsOff);
+    j.errw = reinterpret_cast<int*>(c->xmem + kErrOff);
+    j.buf = own;
+    j.y = y;
+    j.count = (int64_t)count;
+    j.epoch = e;
+    j.limit_ns = (long long)(c->join_timeout_s * 1e9);
+    j.world = c->world;
+    j.rank = c->rank;
+    j.reduce = column ? 0 : 1;
+    j.vec4 = (count % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) ? 1 : 0;
+    const int64_t items = j.vec4 ? (int64_t)count / 4 : (int64_t)count;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, 148 * 2));
+    qmm::note_launch();
+    tp_join_kernel<<<blocks, 256, 0, st>>>(j);
+    const cudaError_t e2 = cudaGetLastError();
+    if (e2 != cudaSuccess) {
+        abort_comm(c);
+        return fail(QMM_ERR_CUDA, std::string("tp_join_kernel: ") + cudaGetErrorString(e2));
+    }
+    c->epoch = e;
+    c->peer_used = true;
     return QMM_OK;
 }
 
@@ -295,6 +510,7 @@ QMM_API int qmm_tp_destroy(qmm_tp_comm* c) {
             if (!c->aborted.load()) nccl().CommDestroy(c->comm);
         }
         if (c->gbuf) cudaFree(c->gbuf);
+        release_peer(c);
     }
     delete c;
     return rc;
@@ -304,6 +520,76 @@ QMM_API int qmm_tp_rank(const qmm_tp_comm* c, int* rank, int* world) {
     if (!c) return fail(QMM_ERR_INVALID_INPUT, "null communicator");
     if (rank) *rank = c->rank;
     if (world) *world = c->world;
+    return QMM_OK;
+}
+
+QMM_API int qmm_tp_enable_peer(qmm_tp_comm* c, size_t bytes, double join_timeout_s) {
+    int rc = usable(c);
+    if (rc) return rc;
+    if (bytes == 0) return fail(QMM_ERR_INVALID_INPUT, "join buffers must not be empty");
+    if (c->world > qmm::kMaxPeers) return fail(QMM_ERR_INVALID_INPUT, "peer joins take at most 8 ranks");
+    if (c->peer_on) return fail(QMM_ERR_INVALID_INPUT, "peer joins are already enabled");
+    DevGuard guard(c->device);
+    if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    c->cap = align256(bytes);
+    c->join_timeout_s = join_timeout_s > 0.0 ? join_timeout_s : c->timeout_s;
+    const size_t total = kBufOff + 2 * c->cap;
+    auto cuda_err = [&](cudaError_t e, const char* what) {
+        cudaGetLastError();
+        release_peer(c);
+        return fail(QMM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    };
+    cudaError_t e = cudaMalloc(&c->xmem, total);
+    if (e != cudaSuccess) {
+        c->xmem = nullptr;
+        return cuda_err(e, "join buffers");
+    }
+    // zeroed before this rank's handle leaves: no peer can write earlier
+    e = cudaMemset(c->xmem, 0, total);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_err(e, "join buffers");
+    c->pmem[c->rank] = c->xmem;
+    if (c->world == 1) {
+        c->peer_on = true;
+        return QMM_OK;
+    }
+    cudaIpcMemHandle_t mine;
+    e = cudaIpcGetMemHandle(&mine, c->xmem);
+    if (e != cudaSuccess) return cuda_err(e, "cudaIpcGetMemHandle");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    uint8_t* dh = nullptr;
+    cudaStream_t s = nullptr;
+    e = cudaMalloc(&dh, hb * (size_t)c->world);
+    if (e == cudaSuccess) e = cudaMemcpy(dh + hb * (size_t)c->rank, &mine, hb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        if (dh) cudaFree(dh);
+        return cuda_err(e, "handle exchange");
+    }
+    // the handles travel through the communicator itself (bounded like every wait)
+    rc = enqueued(c, nccl().AllGather(dh + hb * (size_t)c->rank, dh, hb, ncclUint8, c->comm, s), "ncclAllGather");
+    if (!rc) rc = qmm_tp_wait(c, s, c->timeout_s);
+    std::vector<cudaIpcMemHandle_t> all((size_t)c->world);
+    if (!rc) {
+        e = cudaMemcpy(all.data(), dh, hb * (size_t)c->world, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = fail(QMM_ERR_CUDA, std::string("handle exchange: ") + cudaGetErrorString(e));
+    }
+    cudaStreamDestroy(s);
+    cudaFree(dh);
+    if (rc) {
+        release_peer(c);
+        return rc;
+    }
+    for (int r = 0; r < c->world; ++r) {
+        if (r == c->rank) continue;
+        void* p = nullptr;
+        e = cudaIpcOpenMemHandle(&p, all[(size_t)r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_err(e, "cudaIpcOpenMemHandle");
+        c->pmem[r] = static_cast<uint8_t*>(p);
+    }
+    c->epoch = 0;
+    c->peer_on = true;
     return QMM_OK;
 }
 
@@ -343,7 +629,24 @@ QMM_API int qmm_tp_wait(qmm_tp_comm* c, void* stream, double timeout_s) {
             return fail(QMM_ERR_NCCL, "communicator error: " + nccl_str(r != ncclSuccess ? r : as));
         }
         const cudaError_t q = cudaStreamQuery(st);
-        if (q == cudaSuccess) return QMM_OK;
+        if (q == cudaSuccess) {
+            if (!c->peer_used) return QMM_OK;
+            // a join's bounded wait for a peer's signal records its time-out here
+            int ew = 0;
+            cudaError_t ce = cudaMemcpyAsync(&ew, c->xmem + kErrOff, sizeof(int), cudaMemcpyDeviceToHost, st);
+            if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+            if (ce != cudaSuccess) {
+                cudaGetLastError();
+                return fail(QMM_ERR_CUDA, std::string("join error word: ") + cudaGetErrorString(ce));
+            }
+            c->peer_used = false;
+            if (ew != 0) {
+                abort_comm(c);
+                return fail(QMM_ERR_TIMEOUT, "peer join: a peer's signal did not arrive within " +
+                                                 std::to_string(c->join_timeout_s) + " s; communicator aborted");
+            }
+            return QMM_OK;
+        }
         if (q != cudaErrorNotReady) {
             cudaGetLastError();
             return fail(QMM_ERR_CUDA, std::string("cudaStreamQuery: ") + cudaGetErrorString(q));
@@ -395,6 +698,8 @@ QMM_API int qmm_tp_column_forward(qmm_tp_comm* c, const qmm_weight* shard, const
     if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
     const cudaStream_t st = (cudaStream_t)stream;
     if (c->world == 1) return qmm_linear_forward(shard, x, m, y, act, stream);
+    rc = peer_forward(c, shard, x, m, y, act, st, /*column=*/true, nl);
+    if (rc != -1) return rc;
     if (m == 1) {
         // [1][world * nl] is already rank-major: gather in place
         float* slot = y + (size_t)c->rank * nl;
@@ -433,6 +738,10 @@ QMM_API int qmm_tp_row_forward(qmm_tp_comm* c, const qmm_weight* shard, const fl
     if (m == 0) return QMM_OK;
     DevGuard guard(c->device);
     if (!guard.ok) return fail(QMM_ERR_CUDA, "cudaSetDevice failed");
+    if (c->world > 1) {
+        rc = peer_forward(c, shard, x_local, m, y, act, (cudaStream_t)stream, /*column=*/false, n);
+        if (rc != -1) return rc;
+    }
     rc = qmm_linear_forward(shard, x_local, m, y, act, stream);
     if (rc || c->world == 1) return rc;
     return enqueued(c, nccl().AllReduce(y, y, m * n, ncclFloat32, ncclSum, c->comm, (cudaStream_t)stream),

@@ -127,6 +127,14 @@ class TpComm:
     def handle(self) -> ctypes.c_void_p:
         return self._h
 
+    def enable_peer(self, nbytes: int, join_timeout_s: float = 0.0) -> None:
+        """Joins over peer memory (qmm_tp_enable_peer): column / row forwards
+        whose joined result fits in `nbytes` are written straight into every
+        rank's buffer over NVLink and joined by one flag-barrier kernel instead
+        of an NCCL collective; a join waits at most `join_timeout_s` for the
+        peers (<= 0: the communicator's limit). Collective: every rank calls it."""
+        _lib.check(_lib.lib().qmm_tp_enable_peer(self._h, int(nbytes), float(join_timeout_s)))
+
     def status(self) -> int:
         """One poll of the communicator's error state (a status code, never raises)."""
         return _lib.lib().qmm_tp_status(self._h)

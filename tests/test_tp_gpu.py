@@ -126,7 +126,38 @@ def _worker(rank: int, world: int, port: int):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     comm = TpComm.from_group(rank, timeout_s=60.0)
     oracle.build()
-    for dt, m, k, n in [(Q4_0, 1, 1152, 6912), (Q8_0, 8, 6912, 1152), (Q4_0, 32, 8192, 512)]:
+    _parity_pass(comm, rank, oracle, assert_close_rel, GELU)
+    # the same joins over peer memory: band GEMV (M = 1, 16384 x 8192) and
+    # f16 GEMM (M = 32) epilogues store into every rank's buffer over NVLink,
+    # the other kernels' results are pushed by a copy kernel; one flag-barrier
+    # kernel per call. Column results stay bit-identical to one GPU.
+    comm.enable_peer(64 << 20)
+    _parity_pass(comm, rank, oracle, assert_close_rel, GELU,
+                 extra=[(Q4_0, 1, 8192, 16384), (Q8_0, 1, 4096, 8192), (Q4_0, 32, 8192, 2048), (Q8_0, 32, 4096, 4096)])
+    # a join whose peer never signals: rank 0 runs a row-parallel forward that
+    # rank 1 skips (a dropped message); rank 0's bounded wait runs out and the
+    # next wait returns QMM_ERR_TIMEOUT. Rank 1 stays alive until rank 0's
+    # kernels are done (the gloo barrier), so no write reaches freed memory.
+    short = TpComm.from_group(rank, timeout_s=60.0)
+    short.enable_peer(1 << 20, join_timeout_s=2.0)
+    w = _weights(oracle, Q8_0, 256, 1024, seed=5)
+    row = RowParallelLinear(Q8_0, 256, 1024, w, rank, short)
+    xs = torch.ones(1, 512, device="cuda")
+    if rank == 0:
+        row.forward_local(xs)
+        rc = short.wait(30.0)
+        assert rc == ERR_TIMEOUT, rc
+    torch.cuda.synchronize()
+    dist.barrier()
+    short.abort()
+    short.close()
+    _leave_test(comm, rank, world, StepGuard, default_store)
+
+
+def _parity_pass(comm, rank, oracle, assert_close_rel, GELU, extra=()):
+    from machinelearning_b200.tp import ColumnParallelLinear, ParallelFeedForward, RowParallelLinear
+
+    for dt, m, k, n in [(Q4_0, 1, 1152, 6912), (Q8_0, 8, 6912, 1152), (Q4_0, 32, 8192, 512), *extra]:
         w = _weights(oracle, dt, n, k, seed=k + n + m)
         x = np.random.default_rng(m).normal(0, 1, (m, k)).astype(np.float32)
         xd = torch.from_numpy(x).cuda()
@@ -179,6 +210,9 @@ def _worker(rank: int, world: int, port: int):
             ref = decode_step(cfg, hw, tokens, pos, kc, vc)
             assert_close_rel(got.cpu().numpy().ravel(), ref.ravel(), 1e-3)
         dec.close()
+
+
+def _leave_test(comm, rank, world, StepGuard, default_store):
     # rank 1 leaves between steps; rank 0 learns it on the host, launches nothing
     guard = StepGuard(default_store(), rank, world, timeout_s=3.0, prefix="tp_gpu_leave")
     buf = torch.ones(1024, device="cuda")

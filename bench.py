@@ -396,20 +396,21 @@ def run_ours(args, rank, world, local_rank):
         else:
             torch.cuda.synchronize(dev)
 
-    # ---- CUDA graphs (one GPU) ---------------------------------------------------------------
+    # ---- CUDA graphs ---------------------------------------------------------------------------
     # A timed region of K steps runs step i on weight copy i % copies: whole
     # passes over the copies as one graph each, then one graph of the
     # remaining K % copies steps (copies 0, 1, ...), so a region is at most
-    # K // copies + 1 graph launches whatever K is. With N GPUs the steps are
-    # enqueued directly: the library's NCCL communicator is non-blocking (its
-    # launches may complete on NCCL's own thread), which stream capture does
-    # not take.
+    # K // copies + 1 graph launches whatever K is. With N GPUs the joins over
+    # peer memory are plain kernels and are captured the same way; NCCL joins
+    # (--join nccl) are enqueued directly: the library's NCCL communicator is
+    # non-blocking (its launches may complete on NCCL's own thread), which
+    # stream capture does not take.
     graphs = {}
     with torch.cuda.stream(stream):
         for c in range(copies):
             one_step(c)  # warm the planner/tensor-map caches outside capture
         sync()
-    if comm is not None:
+    if comm is not None and args.join != "peer":
         n0 = L.qmm_launch_count()
         with torch.cuda.stream(stream):
             one_step(0)
@@ -516,7 +517,8 @@ def run_ours(args, rank, world, local_rank):
                 "algorithmic_flops_per_step": sum(2 * gemvs_of(kind) * b * k * n for b in wl["batches"]
                                                   for (_, kl, nl, dt, kind, k, n) in problems),
                 "graph": ("one CUDA graph per pass over the weight copies plus one for the remaining K % copies "
-                          "steps; PDL between kernels" if comm is None else
+                          "steps (joins over peer memory captured with them); PDL between kernels"
+                          if comm is None or args.join == "peer" else
                           "direct launches (non-blocking NCCL communicator; no stream capture); PDL between kernels"),
             },
             "roofline": {
@@ -821,6 +823,7 @@ def run_decode(args, rank, world, local_rank, shared=None):
     model.wait(120.0)
     launches = int(L.qmm_launch_count() - n0)
     model.capture(advance=False)
+    graphed = model.graph is not None
     st = model.stream
 
     def enqueue(n):
@@ -875,8 +878,9 @@ def run_decode(args, rank, world, local_rank, shared=None):
         e2e = {"value": round(B * (1 if tp else world) * k / dt_s, 2), "unit": "tokens/s",
                "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * cfg.vocab * 4, "steps": k,
                "ms_per_step": round(dt_s * 1e3 / k, 4),
-               "path": ("pinned host token ids -> the decode step (graph replay; sharded: direct launches and the "
-                        "communicator's wait) -> pinned host logits, synchronous")}
+               "path": ("pinned host token ids -> the decode step (" +
+                        ("graph replay" if graphed else "direct launches") +
+                        ("; sharded: the communicator's wait" if tp else "") + ") -> pinned host logits, synchronous")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -903,8 +907,11 @@ def run_decode(args, rank, world, local_rank, shared=None):
                                        f"replicated (libqmm communicator, "
                                        f"{'joins over peer memory' if args.join == 'peer' else 'NCCL joins'})" if tp else
                                        (f"{world} replicas" if world > 1 else "single")),
-                       "graph": ("direct launches (sharded step: the non-blocking communicator is not captured)"
-                                 if tp else "one CUDA graph per step (embedding, 26 layers, final norm, lm_head)"),
+                       "graph": ("one CUDA graph per step (embedding, 26 layers, final norm, lm_head)"
+                                 + (", joins over peer memory captured" if tp else "")
+                                 if graphed else
+                                 "direct launches (sharded step with NCCL joins: the non-blocking communicator is "
+                                 "not captured)"),
                        "l2": "weights 0.71 GB > L2", "bytes_per_step": step_bytes},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,

@@ -250,6 +250,8 @@ void take_peer_out(PeerDst& out, bool supported) {
     for (int r = 0; r < kMaxPeers; ++r) out.dst[r] = r < p->n ? p->dst[r] : nullptr;
     out.n = p->n;
     out.ld = p->ld;
+    out.pstride = p->pstride;
+    out.epoch = p->epoch;
     p->taken = true;
 }
 }  // namespace qmm

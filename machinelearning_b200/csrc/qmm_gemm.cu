@@ -657,6 +657,7 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
         // rank's buffer (peer memory over NVLink) instead of y; the launcher
         // offers it only for 16-byte aligned destinations and rows
         const int nout = a.peer.n > 0 ? a.peer.n : 1;
+        const int64_t boff = a.peer.n > 0 ? peer_buffer_offset(a.peer) : 0;
         for (int c4 = lane; c4 < W / 4; c4 += 32)
         for (int r = warp - 2; r < T * BMk && store && a.gact < 0; r += kDqWarps) {
             const int n = n0 + 4 * c4;
@@ -666,7 +667,8 @@ __global__ void __launch_bounds__(gemm_threads(W), 1) gemm_kernel(const __grid_c
             const float4 v = *reinterpret_cast<const float4*>(ys + r * YP + 4 * c4);
             const float4 o = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
             for (int q = 0; q < nout; ++q) {
-                float* yr = a.peer.n > 0 ? a.peer.dst[q] + (int64_t)m * a.peer.ld + n : a.y + (int64_t)m * a.N + n;
+                float* yr = a.peer.n > 0 ? a.peer.dst[q] + boff + (int64_t)m * a.peer.ld + n
+                                         : a.y + (int64_t)m * a.N + n;
                 if ((vec || a.peer.n > 0) && n + 3 < a.N) {
                     *reinterpret_cast<float4*>(yr) = o;
                 } else {

@@ -276,10 +276,11 @@ __global__ void __launch_bounds__(BandThreads<kBandWarps>::kTotal, 1)
             } else if (a.peer.n > 0) {
                 // tensor-parallel join: the same row of every rank's buffer
                 // (peer memory over NVLink), coalesced 128-byte warp stores
+                const int64_t boff = peer_buffer_offset(a.peer);
 #pragma unroll
                 for (int r = 0; r < kMaxPeers; ++r)
                     if (r < a.peer.n) {
-                        float* d = a.peer.dst[r];
+                        float* d = a.peer.dst[r] + boff;
 #pragma unroll
                         for (int m = 0; m < 8; ++m)
                             if (m < a.M && n < a.N) d[(int64_t)m * a.peer.ld + n] = v[m];

@@ -25,14 +25,18 @@ struct GatedOut {
 // Output of a tensor-parallel join written from the producing kernel's own
 // epilogue (qmm_tp.cu): while a request is set on the calling thread, a
 // launcher that supports it (the band GEMV and the f16 GEMM, plain outputs)
-// stores element (m, n) at dst[r] + m * ld + n for every rank r -- peer
-// memory over NVLink, this rank's own buffer among them -- instead of y, and
-// sets `taken`. Other kernels write y and leave it unset.
+// stores element (m, n) at dst[r] + b * pstride + m * ld + n for every rank r
+// -- peer memory over NVLink, this rank's own buffer among them -- instead of
+// y, and sets `taken`; b = (*epoch + 1) & 1 is the join's buffer, read on the
+// device so that a captured step replays correctly. Other kernels write y
+// and leave it unset.
 constexpr int kMaxPeers = 8;
 struct PeerOut {
     float* dst[kMaxPeers] = {};
     int n = 0;
     int64_t ld = 0;
+    int64_t pstride = 0;
+    const unsigned long long* epoch = nullptr;
     bool taken = false;
 };
 PeerOut* peer_out();  // this thread's request (null: none)
@@ -42,7 +46,14 @@ struct PeerDst {
     float* dst[kMaxPeers];
     int n;
     int64_t ld;
+    int64_t pstride;
+    const unsigned long long* epoch;
 };
+// Element offset of the join's buffer (device side; the preceding join has
+// completed before any epilogue runs: stream order / programmatic wait).
+__device__ __forceinline__ int64_t peer_buffer_offset(const PeerDst& p) {
+    return (int64_t)((__ldcg(p.epoch) + 1ull) & 1ull) * p.pstride;
+}
 // Takes this thread's request when the launch can honour it (row-contiguous
 // [M][N] output, 16-byte aligned rows for vector stores): fills `out`, marks
 // the request taken. Otherwise `out.n` = 0.

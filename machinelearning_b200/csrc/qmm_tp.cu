@@ -141,8 +141,11 @@ __global__ void tp_reorder_kernel(const float* __restrict__ g, float* __restrict
 
 // ---- joins over peer memory (qmm_tp_enable_peer) ------------------------------------
 // Every rank owns one allocation, mapped into every other rank's address space
-// (CUDA IPC over NVLink): [flags: one u64 per rank][error word][buffer 0][buffer 1].
-// A join of epoch e writes rank s's part into buffer e % 2 of every rank --
+// (CUDA IPC over NVLink): [flags: one u64 per rank][error word][epoch][ticket]
+// [buffer 0][buffer 1]. The epoch lives on the device: the join kernel reads
+// it, and the last of its CTAs advances it, so a captured sequence of joins
+// replays correctly. A join of epoch e writes rank s's part into buffer e % 2
+// of every rank --
 // from the producing kernel's epilogue (band GEMV, f16 GEMM) or, for other
 // kernels, tp_push_kernel -- then tp_join_kernel stores e into flags[s] of
 // every peer (release, system scope), waits until its own flags[r] >= e for
@@ -151,7 +154,7 @@ __global__ void tp_reorder_kernel(const float* __restrict__ g, float* __restrict
 // holds the same bits). Two buffers suffice: a rank writes epoch e + 1 only
 // after it saw every peer's flag e, which each peer stores after it has read
 // out its epoch e - 1 buffer (stream order).
-constexpr size_t kFlagsOff = 0, kErrOff = 64, kBufOff = 256;
+constexpr size_t kFlagsOff = 0, kErrOff = 64, kEpochOff = 128, kTicketOff = 192, kBufOff = 256;
 
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
     uint64_t v;
@@ -169,19 +172,19 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Copies this rank's [rows][cols] result into every rank's buffer (row stride ld).
 struct PushArgs {
-    float* dst[qmm::kMaxPeers];
+    qmm::PeerDst to;
     const float* src;
-    int64_t rows, cols, ld;
-    int n;
+    int64_t rows, cols;
 };
 __global__ void tp_push_kernel(const __grid_constant__ PushArgs a) {
     const int64_t total = a.rows * a.cols;
+    const int64_t boff = qmm::peer_buffer_offset(a.to);
     for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = o / a.cols, j = o - i * a.cols;
         const float v = a.src[o];
 #pragma unroll
         for (int r = 0; r < qmm::kMaxPeers; ++r)
-            if (r < a.n) a.dst[r][i * a.ld + j] = v;
+            if (r < a.to.n) a.to.dst[r][boff + i * a.to.ld + j] = v;
     }
 }
 
@@ -189,19 +192,23 @@ struct JoinArgs {
     uint64_t* signal[qmm::kMaxPeers];  // &flags[rank] in rank r's allocation (null for this rank)
     const uint64_t* flags;             // this rank's flags
     int* errw;                         // this rank's error word
-    const float* buf;                  // this rank's buffer of the epoch
+    unsigned long long* epoch;         // this rank's epoch (joins completed)
+    unsigned* ticket;                  // CTAs done, zero between joins
+    const float* buf;                  // this rank's buffer 0 (buffer 1 at + pstride)
+    int64_t pstride;
     float* y;
     int64_t count;  // elements of y (row join: also of each rank's slot)
-    uint64_t epoch;
     long long limit_ns;
     int world, rank, reduce, vec4;
 };
 __global__ void tp_join_kernel(const __grid_constant__ JoinArgs a) {
+    // every CTA reads the epoch before the last one to finish advances it
+    const uint64_t e = __ldcg(a.epoch) + 1ull;
     // everything this rank wrote for the epoch precedes this kernel in stream
     // order; the release below publishes it to the peers
     if (blockIdx.x == 0 && threadIdx.x < (unsigned)a.world && (int)threadIdx.x != a.rank) {
         __threadfence_system();
-        st_release_sys(a.signal[threadIdx.x], a.epoch);
+        st_release_sys(a.signal[threadIdx.x], e);
     }
     __shared__ int ok;
     if (threadIdx.x == 0) {
@@ -209,7 +216,7 @@ __global__ void tp_join_kernel(const __grid_constant__ JoinArgs a) {
         const uint64_t t0 = global_ns();
         for (int r = 0; r < a.world && good; ++r) {
             if (r == a.rank) continue;
-            while (ld_acquire_sys(a.flags + r) < a.epoch) {
+            while (ld_acquire_sys(a.flags + r) < e) {
                 if ((long long)(global_ns() - t0) > a.limit_ns) {
                     good = 0;
                     atomicExch(a.errw, 1);
@@ -221,11 +228,13 @@ __global__ void tp_join_kernel(const __grid_constant__ JoinArgs a) {
         ok = good;
     }
     __syncthreads();
-    if (!ok) return;  // y is left as it was; the host reads the error word
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (a.vec4) {
-        const float4* b4 = reinterpret_cast<const float4*>(a.buf);
+    const float* buf = a.buf + (int64_t)(e & 1ull) * a.pstride;
+    if (!ok) {
+        // y is left as it was; the host reads the error word
+    } else if (a.vec4) {
+        const float4* b4 = reinterpret_cast<const float4*>(buf);
         float4* y4 = reinterpret_cast<float4*>(a.y);
         const int64_t n4 = a.count / 4;
         for (int64_t i = t; i < n4; i += stride) {
@@ -241,9 +250,19 @@ __global__ void tp_join_kernel(const __grid_constant__ JoinArgs a) {
         }
     } else {
         for (int64_t i = t; i < a.count; i += stride) {
-            float s = __ldcg(a.buf + i);
-            for (int r = 1; a.reduce && r < a.world; ++r) s += __ldcg(a.buf + r * a.count + i);
+            float s = __ldcg(buf + i);
+            for (int r = 1; a.reduce && r < a.world; ++r) s += __ldcg(buf + r * a.count + i);
             a.y[i] = s;
+        }
+    }
+    // the last CTA to finish advances the epoch (and leaves the ticket zero)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.ticket, 1u) == gridDim.x - 1) {
+            *a.ticket = 0u;
+            *a.epoch = e;
+            __threadfence();
         }
     }
 }
@@ -262,7 +281,6 @@ struct qmm_tp_comm {
     uint8_t* xmem = nullptr;                   // this rank's allocation
     uint8_t* pmem[qmm::kMaxPeers] = {};        // every rank's allocation as mapped here (own included)
     size_t cap = 0;                            // bytes per buffer
-    uint64_t epoch = 0;
     double join_timeout_s = 60.0;              // a join's wait for the peers' signals
     bool peer_on = false;
     bool peer_used = false;                    // a join ran since the last wait
@@ -352,9 +370,8 @@ void release_peer(qmm_tp_comm* c) {
 }
 
 // The join of one column- or row-parallel forward over peer memory. Returns
-// -1 when the join cannot take this call (not enabled, too large for the
-// buffers, or the stream is being captured: the epoch is a launch argument),
-// so the caller joins through NCCL instead.
+// -1 when the join cannot take this call (not enabled, or too large for the
+// buffers), so the caller joins through NCCL instead.
 int peer_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t m, float* y, int act,
                  cudaStream_t st, bool column, size_t cols) {
     if (!c->peer_on) return -1;
@@ -362,23 +379,19 @@ int peer_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t
     const size_t count = column ? m * W * cols : m * cols;
     const size_t need = (column ? count : W * count) * sizeof(float);
     if (need > c->cap) return -1;
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
-        cudaGetLastError();
-        return -1;
-    }
-    const uint64_t e = c->epoch + 1;
-    const size_t par = (size_t)(e & 1) * c->cap;
-    float* own = reinterpret_cast<float*>(c->xmem + kBufOff + par);
+    float* own = reinterpret_cast<float*>(c->xmem + kBufOff);  // buffer 0; buffer 1 at + cap
+    const unsigned long long* epoch = reinterpret_cast<const unsigned long long*>(c->xmem + kEpochOff);
     qmm::PeerOut po;
     po.n = c->world;
     po.ld = column ? (int64_t)(W * cols) : (int64_t)cols;
+    po.pstride = (int64_t)(c->cap / sizeof(float));
+    po.epoch = epoch;
     const size_t part = column ? (size_t)c->rank * cols : (size_t)c->rank * m * cols;  // this rank's place
-    for (int r = 0; r < c->world; ++r) po.dst[r] = reinterpret_cast<float*>(c->pmem[r] + kBufOff + par) + part;
+    for (int r = 0; r < c->world; ++r) po.dst[r] = reinterpret_cast<float*>(c->pmem[r] + kBufOff) + part;
     // where a kernel that cannot write the join itself leaves the result:
-    // contiguous [m][cols]
-    float* ylocal = own + part;
-    if (column && m > 1) {
+    // contiguous [m][cols] (not in the join buffers: their index is on the device)
+    float* ylocal = nullptr;
+    {
         int rc = gather_buffer(c, m * cols * sizeof(float), st, &ylocal);
         if (rc) return rc;
     }
@@ -388,12 +401,14 @@ int peer_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t
     if (rc) return rc;
     if (!po.taken) {
         PushArgs pa;
-        for (int r = 0; r < qmm::kMaxPeers; ++r) pa.dst[r] = po.dst[r];
+        for (int r = 0; r < qmm::kMaxPeers; ++r) pa.to.dst[r] = po.dst[r];
+        pa.to.n = c->world;
+        pa.to.ld = po.ld;
+        pa.to.pstride = po.pstride;
+        pa.to.epoch = epoch;
         pa.src = ylocal;
         pa.rows = (int64_t)m;
         pa.cols = (int64_t)cols;
-        pa.ld = po.ld;
-        pa.n = c->world;
         const int64_t total = pa.rows * pa.cols;
         const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 4);
         qmm::note_launch();
@@ -411,10 +426,12 @@ int peer_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t
                           : nullptr;
     j.flags = reinterpret_cast<const uint64_t*>(c->xmem + kFlagsOff);
     j.errw = reinterpret_cast<int*>(c->xmem + kErrOff);
+    j.epoch = reinterpret_cast<unsigned long long*>(c->xmem + kEpochOff);
+    j.ticket = reinterpret_cast<unsigned*>(c->xmem + kTicketOff);
     j.buf = own;
+    j.pstride = po.pstride;
     j.y = y;
     j.count = (int64_t)count;
-    j.epoch = e;
     j.limit_ns = (long long)(c->join_timeout_s * 1e9);
     j.world = c->world;
     j.rank = c->rank;
@@ -429,7 +446,6 @@ int peer_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t
         abort_comm(c);
         return fail(QMM_ERR_CUDA, std::string("tp_join_kernel: ") + cudaGetErrorString(e2));
     }
-    c->epoch = e;
     c->peer_used = true;
     return QMM_OK;
 }
@@ -588,7 +604,6 @@ QMM_API int qmm_tp_enable_peer(qmm_tp_comm* c, size_t bytes, double join_timeout
         if (e != cudaSuccess) return cuda_err(e, "cudaIpcOpenMemHandle");
         c->pmem[r] = static_cast<uint8_t*>(p);
     }
-    c->epoch = 0;
     c->peer_on = true;
     return QMM_OK;
 }
@@ -630,7 +645,9 @@ QMM_API int qmm_tp_wait(qmm_tp_comm* c, void* stream, double timeout_s) {
         }
         const cudaError_t q = cudaStreamQuery(st);
         if (q == cudaSuccess) {
-            if (!c->peer_used) return QMM_OK;
+            // (captured joins replay without passing through here: with joins
+            // over peer memory enabled, every wait reads the error word)
+            if (!c->peer_on) return QMM_OK;
             // a join's bounded wait for a peer's signal records its time-out here
             int ew = 0;
             cudaError_t ce = cudaMemcpyAsync(&ew, c->xmem + kErrOff, sizeof(int), cudaMemcpyDeviceToHost, st);

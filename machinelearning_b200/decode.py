@@ -269,9 +269,12 @@ class Gemma3Decoder:
 
     def capture(self, advance: bool = True) -> None:
         """Record one step (and, with ``advance``, the position increment) as a
-        CUDA graph; later ``step()`` calls replay it. A sharded decoder keeps
-        launching directly (its communicator is not captured)."""
-        if self.comm:
+        CUDA graph; later ``step()`` calls replay it. A sharded decoder is
+        captured only when every join of the step goes over peer memory
+        (TpComm.enable_peer with room for the logits and the FFN partials);
+        NCCL joins are not captured, so it keeps launching directly."""
+        if self.comm and not self.comm.peer_bytes >= 4 * self.batch * max(
+                self.cfg.vocab, self.comm.world * self.cfg.hidden):
             self.graph = None
             return
         # one direct launch first (it rewrites this position's cache rows with

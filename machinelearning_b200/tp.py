@@ -95,6 +95,7 @@ class TpComm:
     def __init__(self, handle: int, rank: int, world: int, device: int, timeout_s: float):
         self._h = ctypes.c_void_p(handle)
         self.rank, self.world, self.device, self.timeout_s = rank, world, device, timeout_s
+        self.peer_bytes = 0  # join buffer size once enable_peer ran
 
     @staticmethod
     def available() -> bool:
@@ -134,6 +135,7 @@ class TpComm:
         of an NCCL collective; a join waits at most `join_timeout_s` for the
         peers (<= 0: the communicator's limit). Collective: every rank calls it."""
         _lib.check(_lib.lib().qmm_tp_enable_peer(self._h, int(nbytes), float(join_timeout_s)))
+        self.peer_bytes = int(nbytes)
 
     def status(self) -> int:
         """One poll of the communicator's error state (a status code, never raises)."""

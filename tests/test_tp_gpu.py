@@ -204,6 +204,9 @@ def _parity_pass(comm, rank, oracle, assert_close_rel, GELU, extra=()):
         rng = np.random.default_rng(31 + B)  # the same token ids on both ranks
         dec.set_position(0)
         for pos in range(3):
+            if pos == 1 and comm.peer_bytes:
+                dec.capture()  # joins over peer memory: later steps replay one graph
+                assert dec.graph is not None
             tokens = rng.integers(0, cfg.vocab, B)
             got = dec.step(tokens)
             dec.wait(60.0)

@@ -588,8 +588,13 @@ def run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies, comm
 
 def e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, comm):
     """Pinned host x -> device -> the library's forward (the tensor-parallel C
-    ABI for N > 1) -> pinned host y, every projection, one synchronize per step;
-    a Megatron-paired FFN copies in x and copies out down's y only."""
+    ABI for N > 1) -> pinned host y, every projection of every step; a
+    Megatron-paired FFN copies in x and copies out down's y only. Inputs are
+    copied in on the compute stream; each result is copied out on a second
+    stream as soon as its kernel is done, from one of two device buffers (step
+    parity), so the copies of step i overlap the compute of step i + 1 (a
+    serving loop's double buffering). The timed region ends when every step's
+    results are in host memory."""
     import torch
     import torch.distributed as dist
     from machinelearning_b200 import _lib
@@ -600,25 +605,33 @@ def e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, c
     for b in wl["batches"]:
         for pi, (name, kl, nl, dt, kind, k, n) in enumerate(problems):
             out_n = nl * world if kind == "col" else nl
-            dy[(b, pi)] = torch.empty(b, out_n, device=dev)
+            for par in (0, 1):
+                dy[(b, pi, par)] = torch.empty(b, out_n, device=dev)
             if kind == "row_h":
-                dx[(b, pi)] = dy[(b, pi - 1)]
+                for par in (0, 1):
+                    dx[(b, pi, par)] = dy[(b, pi - 1, par)]
             else:
                 hx[(b, pi)] = torch.randn(b, kl).pin_memory()
-                dx[(b, pi)] = torch.empty(b, kl, device=dev)
+                for par in (0, 1):
+                    dx[(b, pi, par)] = torch.empty(b, kl, device=dev)
                 h2d += b * kl * 4
             if kind != "gated":
                 hy[(b, pi)] = torch.empty(b, out_n).pin_memory()
                 d2h += b * out_n * 4
     steps = max(3, min(args.steps, 100))
+    cs = torch.cuda.Stream(dev)  # device -> host copies
+    copied = [None, None]        # per parity: the copy stream's last event of that step
 
-    def step(c):
+    def step(c, i):
+        par = i & 1
         with torch.cuda.stream(stream):
+            if copied[par] is not None:  # step i - 2's results have left these buffers
+                stream.wait_event(copied[par])
             for b in wl["batches"]:
                 for pi, (name, kl, nl, dt, kind, k, n) in enumerate(problems):
                     if (b, pi) in hx:
-                        dx[(b, pi)].copy_(hx[(b, pi)], non_blocking=True)
-                    w, x, y = weights[c][pi].handle, dx[(b, pi)].data_ptr(), dy[(b, pi)].data_ptr()
+                        dx[(b, pi, par)].copy_(hx[(b, pi)], non_blocking=True)
+                    w, x, y = weights[c][pi].handle, dx[(b, pi, par)].data_ptr(), dy[(b, pi, par)].data_ptr()
                     if kind == "gated":
                         _lib.check(L.qmm_gated_forward(w, x, b, y, SILU, sp))
                     elif comm is None:
@@ -628,19 +641,30 @@ def e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, c
                     else:
                         _lib.check(L.qmm_tp_row_forward(comm.handle, w, x, b, y, 0, sp))
                     if (b, pi) in hy:
-                        hy[(b, pi)].copy_(dy[(b, pi)], non_blocking=True)
-            if comm is not None:
-                _lib.check(comm.wait(120.0, stream))
-            else:
-                stream.synchronize()
+                        done = torch.cuda.Event()
+                        done.record(stream)
+                        cs.wait_event(done)
+                        with torch.cuda.stream(cs):
+                            hy[(b, pi)].copy_(dy[(b, pi, par)], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(cs)
+        copied[par] = ev
+
+    def drain():
+        if comm is not None:
+            _lib.check(comm.wait(120.0, stream))
+        cs.synchronize()
+        stream.synchronize()
 
     for i in range(3):
-        step(i % copies)
+        step(i % copies, i)
+    drain()
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
     for i in range(steps):
-        step(i % copies)
+        step(i % copies, i)
+    drain()
     if world > 1:
         dist.barrier()
     dt_s = time.perf_counter() - t0
@@ -653,8 +677,9 @@ def e2e_staged(args, wl, problems, weights, L, sp, stream, world, dev, copies, c
     _, unit, div = metric_info(wl)
     return {"value": round(work_step * steps / dt_s / div, 1), "unit": unit, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(dt_s * 1e3 / steps, 4),
-            "path": ("pinned host x -> the library's forward on this rank's shard (qmm_tp_* NCCL join for N > 1) -> "
-                     "pinned host y, one wait per step")}
+            "path": ("pinned host x -> the library's forward on this rank's shard (qmm_tp_* join for N > 1) -> "
+                     "pinned host y on a copy stream (two device buffers: step i's copies overlap step i + 1's "
+                     "compute); the region ends when every step's results are in host memory")}
 
 
 # ---- CPU: the reference path restated (oracle/) -------------------------------------------

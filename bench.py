@@ -325,7 +325,7 @@ def run_ours(args, rank, world, local_rank):
         # (column: [batch][N]; row: every rank's [batch][N] partial)
         cap = max(4 * b * (n if kind in ("col", "gated") else world * n)
                   for b in wl["batches"] for (_, kl, n_l, dt, kind, k, n) in problems)
-        comm.enable_peer(cap)
+        enable_peer_or_nccl(comm, cap, args)
 
     gen = torch.Generator(device=dev)
 
@@ -546,6 +546,26 @@ def run_ours(args, rank, world, local_rank):
     del weights, xs, ys
     torch.cuda.empty_cache()
     return line
+
+
+def enable_peer_or_nccl(comm, nbytes, args):
+    """Joins over peer memory; if their setup fails on this machine (no peer
+    access, IPC refused), every rank falls back to NCCL joins together."""
+    import torch
+    import torch.distributed as dist
+    from machinelearning_b200 import _lib
+    ok = 1
+    try:
+        comm.enable_peer(nbytes)
+    except _lib.QmmError as e:
+        print(f"peer joins unavailable ({e}); joining with NCCL", file=sys.stderr, flush=True)
+        ok = 0
+    t = torch.tensor([ok])
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    if int(t.item()) == 0:
+        args.join = "nccl"
+        if ok:  # this rank's peer buffers stay unused: the forwards join through NCCL
+            raise RuntimeError("a peer rank could not set up peer joins; restart with --join nccl")
 
 
 def run_e2e(args, wl, problems, weights, L, sp, stream, world, dev, copies, comm):
@@ -835,7 +855,7 @@ def run_decode(args, rank, world, local_rank, shared=None):
     cfg, w = shared if shared is not None else _decode_weights(local_rank, 0 if tp else rank)
     comm = TpComm.from_group(local_rank, timeout_s=120.0) if tp else None
     if comm is not None and args.join == "peer":
-        comm.enable_peer(4 * args.batch * max(cfg.vocab, world * cfg.hidden))
+        enable_peer_or_nccl(comm, 4 * args.batch * max(cfg.vocab, world * cfg.hidden), args)
     model = Gemma3Decoder(cfg, w, batch=args.batch, device=local_rank, comm=comm)
     L = _lib.lib()
     dev = model.dev

@@ -23,7 +23,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 FAKE_SRC = os.path.join(ROOT, "tests", "fake_nccl", "fake_nccl.c")
-OK, ERR_NCCL, ERR_TIMEOUT, ERR_INVALID_INPUT = 0, 6, 7, 8
+OK, ERR_NCCL, ERR_TIMEOUT, ERR_INVALID_INPUT, ERR_CUDA = 0, 6, 7, 8, 5
 
 
 @pytest.fixture(scope="module")
@@ -78,6 +78,12 @@ res["healthy"] = [rc, L.qmm_tp_rank(h, ctypes.byref(r), ctypes.byref(w)), r.valu
 rc, dt, h = init(0, 5.0)
 res["abort"] = [rc, L.qmm_tp_abort(h), L.qmm_tp_status(h), L.qmm_tp_destroy(h), cnt("fake_nccl_aborts"),
                 cnt("fake_nccl_destroys")]
+# peer joins: argument checks, and a setup that cannot allocate (no GPU here)
+# fails with a status and leaves the communicator usable for NCCL joins
+rc, dt, h = init(0, 5.0)
+res["peer"] = [L.qmm_tp_enable_peer(None, 1024, 0.0), L.qmm_tp_enable_peer(h, 0, 0.0),
+               L.qmm_tp_enable_peer(h, 1 << 20, 0.0), L.qmm_tp_status(h),
+               L.qmm_tp_all_reduce_f32(h, buf, 4, None), L.qmm_tp_destroy(h)]
 res["null"] = [L.qmm_tp_status(None), L.qmm_tp_destroy(None), L.qmm_tp_abort(None)]
 print("RESULT " + json.dumps(res))
 """
@@ -104,6 +110,7 @@ def test_communicator_control_with_stand_in_nccl(fake_nccl):
     assert res["healthy"] == [OK, OK, 0, 2, OK, OK, 1, 1, 0], res["healthy"]
     assert res["abort"] == [OK, OK, ERR_NCCL, OK, 1, 0], res["abort"]
     assert res["null"] == [ERR_INVALID_INPUT, OK, ERR_INVALID_INPUT]
+    assert res["peer"] == [ERR_INVALID_INPUT, ERR_INVALID_INPUT, ERR_CUDA, OK, OK, OK], res["peer"]
 
 
 # ---- StepGuard on gloo ranks ---------------------------------------------------------------------

@@ -283,7 +283,6 @@ struct qmm_tp_comm {
     size_t cap = 0;                            // bytes per buffer
     double join_timeout_s = 60.0;              // a join's wait for the peers' signals
     bool peer_on = false;
-    bool peer_used = false;                    // a join ran since the last wait
 };
 
 namespace {
@@ -446,7 +445,6 @@ int peer_forward(qmm_tp_comm* c, const qmm_weight* shard, const float* x, size_t
         abort_comm(c);
         return fail(QMM_ERR_CUDA, std::string("tp_join_kernel: ") + cudaGetErrorString(e2));
     }
-    c->peer_used = true;
     return QMM_OK;
 }
 
@@ -656,7 +654,6 @@ QMM_API int qmm_tp_wait(qmm_tp_comm* c, void* stream, double timeout_s) {
                 cudaGetLastError();
                 return fail(QMM_ERR_CUDA, std::string("join error word: ") + cudaGetErrorString(ce));
             }
-            c->peer_used = false;
             if (ew != 0) {
                 abort_comm(c);
                 return fail(QMM_ERR_TIMEOUT, "peer join: a peer's signal did not arrive within " +

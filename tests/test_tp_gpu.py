@@ -10,9 +10,13 @@ Two GPUs (skipped with fewer): the column-parallel, row-parallel and
 Megatron-paired feed-forward and the sharded Gemma-3 decode step against the
 oracle's single-process result
 (column-parallel Q8_0-activation outputs bit-exact; f32 outputs and sums within
-the 1e-3 contract), then a rank that leaves between steps: the other learns it
-on the host (StepGuard) before launching its next collective and returns
-QMM_ERR_TIMEOUT. NVLS is off in these tests.
+the 1e-3 contract), first with NCCL joins, then again with joins over peer
+memory (qmm_tp_enable_peer: band GEMV and f16 GEMM epilogues writing every
+rank's buffer, the copy kernel for the rest, a sharded decode step replayed
+from a captured graph); a peer join whose peer never signals returns
+QMM_ERR_TIMEOUT after its 2 s limit; then a rank that leaves between steps:
+the other learns it on the host (StepGuard) before launching its next
+collective and returns QMM_ERR_TIMEOUT. NVLS is off in these tests.
 """
 from __future__ import annotations
 
